@@ -1,0 +1,520 @@
+"""Encoder-attention benchmark: audio-seconds per second through the attention plugins.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload parakeet|zipformer]
+    python bench.py --impl reference ...   # the reference math on the host cores
+
+A *step* is one encoder forward's worth of attention calls over one batch:
+* ``parakeet`` (default): 24 Conformer layers of
+  ``parakeet_relative_attention`` on 256 utterances x 375 frames, fp16, 8 x 128 heads,
+  each layer with its own inputs (590 MB of QKV per layer, far above the 126 MB L2).
+* ``zipformer``: every layer of the six Zipformer stacks
+  (2/2/4/5/4/2 layers at T = 750/375/188/94/188/375), each layer one
+  ``zipformer_relative_attention`` call plus three ``zipformer_attention_value`` calls,
+  bf16, 256 utterances.
+
+``value`` = audio seconds of all ranks' batches x K / max-over-ranks device time of the
+K steps (CUDA events, inputs resident in HBM). ``e2e`` = the same metric through the
+public operator API with host (pinned) inputs copied in and the outputs copied out
+inside the timed region. Under torchrun each rank runs its own batches (weak scaling,
+no collective on the data path; one barrier and one max-reduction of the timings).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+METRIC = "encoder-attention audio-sec/sec (RTFx)"
+UNIT = "audio-s/s"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--workload", choices=("parakeet", "zipformer"), default="parakeet")
+    p.add_argument("--batch", type=int, default=256)
+    p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.is_file():
+        d = json.loads(path.read_text())
+        return dict(hbm_gbs=d["hbm_gbs"], bf16_tflops=d["bf16_tflops"],
+                    bf16_tflops_sustained=d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                    source="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0,
+                source="fallback")
+
+
+def load_traffic(kernel_key: str):
+    """Per-launch DRAM bytes of ``kernel_key`` from the committed ncu summary, or None."""
+    path = REPO / "profiles" / "dram_traffic.txt"
+    if not path.is_file():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel_key and not line.startswith("#"):
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+# ---- clocks sampling ------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus_id = (bus_id or "").lower()
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"fga_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) < 9:
+                continue
+            rows.append(parts)
+        if self.bus_id:
+            mine = [r for r in rows if r[0].lower() == self.bus_id]
+            rows = mine or [r for r in rows if r[0] == rows[0][0]]
+        elif rows:
+            rows = [r for r in rows if r[0] == rows[0][0]]
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+# ---- distributed plumbing -----------------------------------------------------------------
+def init_dist(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "ours":
+        torch.cuda.set_device(local)
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+
+        dist.init_process_group(backend="nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---- workloads -----------------------------------------------------------------------------
+def build_parakeet(args, rank):
+    import torch
+
+    from fast_gpu_asr_b200 import workloads as wl
+
+    layers = []
+    for i in range(wl.PARAKEET_LAYERS):
+        lens = wl.parakeet_lengths(args.batch, 375, 60, seed=1000 * rank + 7)
+        layers.append(wl.make_parakeet_layer(args.batch, 375, 8, 128, torch.float16, "cuda",
+                                             seed=1000 * rank + i, lengths=lens))
+    torch.cuda.synchronize()
+    audio = wl.parakeet_audio_seconds(layers[0].valid_lengths)
+    flops = wl.parakeet_flops(layers[0].valid_lengths, 375, 8, 128)
+    nbytes = wl.parakeet_bytes(args.batch, 375, 8, 128, 2)
+    outs = [torch.empty((args.batch, 375, 1024), dtype=torch.float16, device="cuda")
+            for _ in range(2)]
+    return layers, outs, audio, flops, nbytes
+
+
+def run_parakeet_step(layers, outs, stream, events=None):
+    from fast_gpu_asr_b200.attention import parakeet_relative_attention
+
+    for i, L in enumerate(layers):
+        if events is not None:
+            events[i][0].record(stream)
+        parakeet_relative_attention(L.qkv, L.position, L.content_bias, L.position_bias,
+                                    L.valid_lengths, L.scale, out=outs[i % 2], stream=stream)
+        if events is not None:
+            events[i][1].record(stream)
+
+
+def build_zipformer(args, rank):
+    import torch
+
+    from fast_gpu_asr_b200 import workloads as wl
+
+    input_lengths = wl.zipformer_input_lengths(args.batch, seed=1000 * rank + 1)
+    stacks = []
+    total_bytes = 0.0
+    seed = 1000 * rank
+    for ds, t, embed, heads, nlayers in wl.ZIPFORMER_STACKS:
+        lens = wl.zipformer_stack_lengths(input_lengths, ds)
+        weights = torch.empty((args.batch, heads, t, t), dtype=torch.bfloat16, device="cuda")
+        layers = []
+        for _ in range(nlayers):
+            seed += 1
+            L = wl.make_zipformer_layer(args.batch, t, embed, heads, torch.bfloat16, "cuda",
+                                        seed, lens)
+            layers.append(L)
+            total_bytes += wl.zipformer_layer_bytes(args.batch, t, embed, heads, 2)
+        outs = (torch.empty_like(layers[0].value_a), torch.empty_like(layers[0].nonlin_value))
+        stacks.append((heads, weights, layers, outs))
+    torch.cuda.synchronize()
+    return stacks, wl.zipformer_audio_seconds(input_lengths), total_bytes
+
+
+def run_zipformer_step(stacks, stream, events=None):
+    from fast_gpu_asr_b200.attention import zipformer_attention_value, zipformer_relative_attention
+
+    j = 0
+    for heads, weights, layers, (out_self, out_nl) in stacks:
+        for L in layers:
+            if events is not None:
+                events[j][0].record(stream)
+            zipformer_relative_attention(L.projection, L.position, L.mask, out=weights,
+                                         stream=stream)
+            if events is not None:
+                events[j][1].record(stream)
+            zipformer_attention_value(weights, L.value_a, heads, out=out_self, stream=stream)
+            zipformer_attention_value(weights, L.value_b, heads, out=out_self, stream=stream)
+            zipformer_attention_value(weights, L.nonlin_value, 1, out=out_nl, stream=stream)
+            j += 1
+
+
+# ---- CPU legs (oracle port of the reference math) -----------------------------------------
+def cpu_parakeet(seconds: float):
+    """Time the oracle (reference math restated on torch CPU) on config-2 utterances."""
+    import torch
+
+    from fast_gpu_asr_b200 import workloads as wl
+    from oracle import parakeet_relative_attention as oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    per_call = 4
+    layer = wl.make_parakeet_layer(per_call, 375, 8, 128, torch.float16, "cpu", seed=11)
+    args = dict(qkv=layer.qkv.float().numpy(), position=layer.position.float().numpy(),
+                content_bias=layer.content_bias.float().numpy(),
+                position_bias=layer.position_bias.float().numpy(),
+                valid_lengths=layer.valid_lengths.numpy())
+    oracle(**args, scale=layer.scale, dtype="float16")  # warm-up
+    audio = wl.parakeet_audio_seconds(layer.valid_lengths)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        oracle(**args, scale=layer.scale, dtype="float16")
+        calls += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    value = audio * calls / (elapsed * wl.PARAKEET_LAYERS)
+    sample = (f"{calls} calls x {per_call} utterances x 375 frames (8x128 heads, fp16 "
+              f"rounding) = {calls} of the 24 per-forward layer calls on a {per_call}-utterance "
+              f"slice; scaled to a 24-layer forward")
+    return value, torch.get_num_threads(), sample
+
+
+def cpu_zipformer(seconds: float):
+    import torch
+
+    from fast_gpu_asr_b200 import workloads as wl
+    from oracle import zipformer_attention_value, zipformer_relative_attention
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    per_call = 2
+    input_lengths = wl.zipformer_input_lengths(per_call, seed=3)
+    layers = []
+    for ds, t, embed, heads, nlayers in wl.ZIPFORMER_STACKS:
+        lens = wl.zipformer_stack_lengths(input_lengths, ds)
+        L = wl.make_zipformer_layer(per_call, t, embed, heads, torch.bfloat16, "cpu", 3, lens)
+        layers.append((heads, nlayers, {k: getattr(L, k).float().numpy() if k != "mask"
+                                        else L.mask.numpy() for k in
+                                        ("projection", "position", "mask", "value_a", "value_b",
+                                         "nonlin_value")}))
+    t0 = time.perf_counter()
+    forwards = 0.0
+    while True:
+        for heads, nlayers, x in layers:
+            w = zipformer_relative_attention(x["projection"], x["position"], x["mask"], "bfloat16")
+            zipformer_attention_value(w, x["value_a"], heads, "bfloat16")
+            zipformer_attention_value(w, x["value_b"], heads, "bfloat16")
+            zipformer_attention_value(w, x["nonlin_value"], 1, "bfloat16")
+        # One pass covers one layer of each stack; a forward has 2/2/4/5/4/2 layers.
+        forwards += 6.0 / sum(s[4] for s in wl.ZIPFORMER_STACKS)
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    value = wl.zipformer_audio_seconds(input_lengths) * forwards / elapsed
+    sample = (f"{per_call}-utterance slice, one layer of each of the 6 stacks per pass "
+              f"(weights + 2 self AV + nonlin AV, bf16 rounding), scaled to a 19-layer forward")
+    return value, torch.get_num_threads(), sample
+
+
+def reference_arm(args, world, rank):
+    """`--impl reference`: the reference math (oracle port) on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    fn = cpu_parakeet if args.workload == "parakeet" else cpu_zipformer
+    per_step = []
+    for _ in range(args.warmup):
+        fn(min(2.0, args.cpu_seconds))
+    for _ in range(args.steps):
+        value, cores, sample = fn(args.cpu_seconds / max(1, args.steps) + 0.5)
+        per_step.append(value)
+    value = statistics.median(per_step)
+    config = workload_config(args)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": config["dtype"], "data": "synthetic",
+            "config": config,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    if args.workload == "parakeet":
+        return {"workload": "parakeet_relative_attention (config 2)", "batch": args.batch,
+                "frames": 375, "heads": 8, "head_dim": 128, "layers": 24,
+                "lengths": "U[60,375]", "dtype": "f16", "parallelism": f"dp{args.gpus}",
+                "l2": "inputs exceed L2 (590 MB QKV per layer, 24 distinct layers)"}
+    return {"workload": "zipformer weights + 3 attention-value calls per layer (config 3)",
+            "batch": args.batch, "stacks_T": [750, 375, 188, 94, 188, 375],
+            "layers": [2, 2, 4, 5, 4, 2], "dtype": "bf16", "parallelism": f"dp{args.gpus}",
+            "l2": "weights tensor up to 1.15 GB per layer exceeds L2"}
+
+
+# ---- our arm ---------------------------------------------------------------------------------
+def ours_arm(args, world, rank, local):
+    import torch
+
+    from fast_gpu_asr_b200 import _lib
+
+    _lib.library()
+    peaks = load_peaks()
+    stream = torch.cuda.Stream()
+    dev_props = torch.cuda.get_device_properties(local)
+    bus = getattr(dev_props, "pci_bus_id", None)
+    bus_id = None
+    if bus is not None:
+        bus_id = f"{getattr(dev_props, 'pci_domain_id', 0):08x}:{bus:02x}:{getattr(dev_props, 'pci_device_id', 0):02x}.0"
+
+    if args.workload == "parakeet":
+        layers, outs, audio, flops, nbytes = build_parakeet(args, rank)
+        n_launch = len(layers)
+
+        def step(events=None):
+            run_parakeet_step(layers, outs, stream, events)
+    else:
+        stacks, audio, total_bytes = build_zipformer(args, rank)
+        n_launch = sum(len(s[2]) for s in stacks)
+
+        def step(events=None):
+            run_zipformer_step(stacks, stream, events)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    variant = _lib.last_kernel_variant()
+
+    # Timed region: K steps, with per-launch events around the dominant kernel.
+    events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+               for _ in range(n_launch)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(bus_id) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for k in range(args.steps):
+            step(events[k])
+        end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    barrier(world)
+    elapsed_ms = start.elapsed_time(end)
+    max_ms = allreduce_max(elapsed_ms, world)
+    launch_ms = [e[0].elapsed_time(e[1]) for ev in events for e in ev]
+    avg_launch_ms = float(np.mean(launch_ms))
+
+    total_audio = audio * args.steps * world
+    value = total_audio / (max_ms / 1000.0)
+    ms_per_step = max_ms / args.steps
+
+    if args.workload == "parakeet":
+        achieved = flops / (avg_launch_ms / 1000.0) / 1e12
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                    "traffic": load_traffic("parakeet_relative_attention"),
+                    "peak_source": f"{peaks['source']} bf16 dense (burst)",
+                    "flops_per_launch": flops, "bytes_per_launch": nbytes,
+                    "hbm_frac": nbytes / (avg_launch_ms / 1000.0) / 1e9 / peaks["hbm_gbs"],
+                    "avg_launch_ms": avg_launch_ms, "variant": variant}
+        gpu_launches = args.steps * n_launch
+    else:
+        # The dominant kernel is the weights kernel (writes the NHTT tensor).
+        wbytes = []
+        for heads, weights, layers, outs in stacks:
+            for L in layers:
+                n, t = L.projection.shape[:2]
+                wbytes.append(n * t * heads * 68 * 2 + (2 * t - 1) * heads * 8 + n * t
+                              + weights.numel() * 2)
+        per_launch = np.array(launch_ms).reshape(args.steps, n_launch).mean(axis=0)
+        achieved = float(np.sum(wbytes) / (np.sum(per_launch) / 1000.0) / 1e9)
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                    "traffic": load_traffic("zipformer_relative_attention"),
+                    "peak_source": f"{peaks['source']} HBM copy",
+                    "step_bytes": total_bytes,
+                    "step_hbm_frac": total_bytes / (ms_per_step / 1000.0) / 1e9 / peaks["hbm_gbs"],
+                    "variant": variant}
+        gpu_launches = args.steps * n_launch * 4
+
+    e2e = None
+    if not args.no_e2e and args.workload == "parakeet":
+        e2e = e2e_parakeet(args, layers, audio, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        fn = cpu_parakeet if args.workload == "parakeet" else cpu_zipformer
+        v, cores, sample = fn(args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": workload_config(args)["dtype"], "data": "synthetic",
+                "config": workload_config(args), "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": e2e, "gpu_launches": gpu_launches, "clocks": clocks,
+                "audio_seconds_per_step_per_gpu": audio}
+        print(json.dumps(line), flush=True)
+
+
+def e2e_parakeet(args, layers, audio, world):
+    """Same metric through the public API with pinned host inputs and outputs."""
+    import torch
+
+    from fast_gpu_asr_b200.attention import parakeet_relative_attention
+
+    stream = torch.cuda.Stream()
+    host_in = []
+    for L in layers[:2]:
+        host_in.append({k: getattr(L, k).cpu().pin_memory() for k in
+                        ("qkv", "position", "content_bias", "position_bias", "valid_lengths")})
+    dev = {k: torch.empty_like(getattr(layers[0], k)) for k in host_in[0]}
+    out = torch.empty((args.batch, 375, 1024), dtype=torch.float16, device="cuda")
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in[0].values()) * len(layers)
+    d2h = out.numel() * out.element_size() * len(layers)
+
+    def step():
+        for i in range(len(layers)):
+            src = host_in[i % 2]
+            for k, t in src.items():
+                dev[k].copy_(t, non_blocking=True)
+            parakeet_relative_attention(dev["qkv"], dev["position"], dev["content_bias"],
+                                        dev["position_bias"], dev["valid_lengths"],
+                                        layers[0].scale, out=out, stream=stream)
+            host_out.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    n = max(1, args.e2e_steps)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(n):
+            step()
+        end.record(stream)
+    torch.cuda.synchronize()
+    ms = allreduce_max(start.elapsed_time(end), world)
+    return {"value": audio * n * world / (ms / 1000.0), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n,
+            "ms_per_step": ms / n}
+
+
+def main():
+    args = parse_args()
+    sys.path.insert(0, str(REPO))
+    world, rank, local = init_dist(args)
+    try:
+        if args.impl == "reference":
+            reference_arm(args, world, rank)
+        else:
+            ours_arm(args, world, rank, local)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,23 @@
+"""B200-native (sm_100a) encoder self-attention for fast-gpu-asr.
+
+Drop-in replacement for the reference's three attention TensorRT plugins
+(``parakeet_relative_attention``, ``zipformer_relative_attention``,
+``zipformer_attention_value``): hand-written CUDA kernels behind the C ABI in
+``include/fga_attention.h``, the same plugin identities for TensorRT, and a
+data-parallel batch-sharding launcher.
+"""
+
+from .attention import (  # noqa: F401
+    parakeet_relative_attention,
+    zipformer_attention_value,
+    zipformer_relative_attention,
+)
+from .constants import (  # noqa: F401
+    PARAKEET_RELATIVE_ATTENTION_PLUGIN_NAME,
+    PLUGIN_VERSION,
+    TENSORRT_PLUGIN_NAMESPACE,
+    ZIPFORMER_ATTENTION_VALUE_PLUGIN_NAME,
+    ZIPFORMER_RELATIVE_ATTENTION_PLUGIN_NAME,
+)
+
+__version__ = "0.1.0"

@@ -1,0 +1,62 @@
+// Internal launch interface between the C ABI (fga_capi.cu) and the kernels.
+// Every problem struct holds already-validated shapes; launchers only choose a
+// kernel variant and launch it on the given stream.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace fga {
+
+struct ParakeetProblem {
+    const void* qkv;       // [N, T, 3C]
+    const void* position;  // [1, 2T-1, C]
+    const void* content_bias;   // [H, D]
+    const void* position_bias;  // [H, D]
+    const int32_t* valid_lengths;  // [N]
+    void* output;          // [N, T, C]
+    int32_t batch, length, heads, head_dim;
+    float scale;
+    int32_t dtype;  // fga_data_type
+};
+
+struct ZipformerWeightsProblem {
+    const void* projection;  // [N, T, H*(2qd+4)]
+    const void* position;    // [1, 2T-1, H, 4]
+    const uint8_t* mask;     // [N, T] bool
+    void* weights;           // [N, H, T, T]
+    int32_t batch, length, heads, query_dim;
+    int32_t dtype;
+};
+
+struct ZipformerValueProblem {
+    const void* attention;  // [N, Ha, T, T]
+    const void* value;      // [N, T, C]
+    void* output;           // [N, T, C]
+    int32_t batch, attention_heads, length, channels, value_heads;
+    int32_t dtype;
+};
+
+// Each launcher returns cudaSuccess or the launch error, and records the variant.
+cudaError_t launch_parakeet(const ParakeetProblem& p, cudaStream_t stream, const char** variant);
+cudaError_t launch_zipformer_weights(const ZipformerWeightsProblem& p, cudaStream_t stream,
+                                     const char** variant);
+cudaError_t launch_zipformer_value(const ZipformerValueProblem& p, cudaStream_t stream,
+                                   const char** variant);
+
+// SIMT (CUDA-core) kernels: every dtype and shape the contract accepts.
+cudaError_t launch_parakeet_simt(const ParakeetProblem& p, cudaStream_t stream);
+cudaError_t launch_zipformer_weights_simt(const ZipformerWeightsProblem& p, cudaStream_t stream);
+cudaError_t launch_zipformer_value_simt(const ZipformerValueProblem& p, cudaStream_t stream);
+
+// Tensor-core (tcgen05/TMEM) kernels for f16/bf16. Each returns cudaErrorNotSupported
+// without launching when the problem is outside the kernel's envelope.
+cudaError_t launch_parakeet_tc(const ParakeetProblem& p, cudaStream_t stream);
+cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem& p, cudaStream_t stream);
+cudaError_t launch_zipformer_value_tc(const ZipformerValueProblem& p, cudaStream_t stream);
+
+// True when the current device is sm_100 (the only target of this library).
+bool device_is_sm100();
+
+}  // namespace fga

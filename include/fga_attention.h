@@ -1,0 +1,163 @@
+/*
+ * fga_attention.h - C ABI of the B200 (sm_100a) encoder self-attention library
+ * (libfga_attention.so).
+ *
+ * The three entry points below replace the bodies of the `enqueue` methods of the
+ * reference's three attention TensorRT plugins. Each takes the same tensor
+ * descriptors (type, rank, dims), the same raw device pointers in the same binding
+ * order and the same stream, and returns 0 on success and nonzero on failure, so a
+ * TensorRT shim converts `PluginTensorDesc` to `fga_tensor_desc` one field at a time
+ * and forwards. No torch, TensorRT or CUDA type appears in any signature: a stream is
+ * passed as `void*` (a `cudaStream_t`), device buffers as `void*`.
+ *
+ * Memory: the caller owns every input, output and workspace buffer; no entry point
+ * allocates device memory, and none needs workspace (the `*_workspace_size` queries
+ * return 0). All launches go on the given stream only, so an entry point is safe to
+ * capture in a CUDA graph and safe to call from several host threads on different
+ * streams at once.
+ *
+ * Error behaviour mirrors the reference plugins: descriptors are re-validated on every
+ * call (rank, dtype, cross-input shape relations, 64-bit size arithmetic), a CUDA
+ * error left over from earlier asynchronous work is reported without launching, and
+ * the launch status is returned.
+ */
+#ifndef FGA_ATTENTION_H
+#define FGA_ATTENTION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FGA_API __attribute__((visibility("default")))
+#else
+#define FGA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FGA_ABI_VERSION 1
+#define FGA_MAX_DIMS 8
+
+/* Element types. The values equal TensorRT's nvinfer1::DataType numbering, so a
+ * plugin shim passes `PluginTensorDesc::type` through unchanged. */
+enum fga_data_type {
+    FGA_FLOAT = 0, /* float32 */
+    FGA_HALF = 1,  /* float16 */
+    FGA_INT32 = 3,
+    FGA_BOOL = 4,  /* one byte per element, 0 or 1 */
+    FGA_BF16 = 7,
+};
+
+/* Status codes. Every nonzero value means that nothing was launched, except
+ * FGA_ERROR_LAUNCH, which reports a failed kernel launch. */
+enum fga_status {
+    FGA_SUCCESS = 0,
+    FGA_ERROR_NULL_POINTER = 1,
+    FGA_ERROR_BAD_DESCRIPTOR = 2, /* rank, dtype or format not accepted */
+    FGA_ERROR_BAD_SHAPE = 3,      /* cross-tensor shape relation violated */
+    FGA_ERROR_OVERFLOW = 4,       /* a size product leaves the int32/int64 range */
+    FGA_ERROR_BAD_FIELD = 5,      /* plugin field (scale, num_heads) rejected */
+    FGA_ERROR_PRIOR_CUDA_ERROR = 6,
+    FGA_ERROR_LAUNCH = 7,
+    FGA_ERROR_NO_DEVICE = 8,      /* current device is not sm_100 */
+};
+
+/* Mirrors nvinfer1::PluginTensorDesc minus format (row-major linear is implied). */
+typedef struct fga_tensor_desc {
+    int32_t type;     /* enum fga_data_type */
+    int32_t nb_dims;  /* 1..FGA_MAX_DIMS */
+    int64_t dims[FGA_MAX_DIMS];
+} fga_tensor_desc;
+
+/* --------------------------------------------------------------------------------
+ * parakeet_relative_attention (Transformer-XL relative-position MHSA, FastConformer)
+ *
+ * Replaces ParakeetRelativeAttentionPlugin::enqueue,
+ *   src/fast_gpu_asr/tensorrt_plugins/parakeet_relative_attention_plugin.cu:923-1139,
+ * with the shape contract of haveValidShapes (same file :237-290) and the field
+ * contract of the creator (:1189-1220).
+ *
+ * inputs[0] qkv            [N, T, 3C]  f32|f16|bf16   (Q heads, K heads, V heads)
+ * inputs[1] position       [1, 2T-1, C] same type     (linear_pos(pos_emb))
+ * inputs[2] content_bias   [H, D]       same type     (pos_bias_u)
+ * inputs[3] position_bias  [H, D]       same type     (pos_bias_v)
+ * inputs[4] valid_lengths  [N]          int32
+ * outputs[0] output        [N, T, C]    same type, C = H*D
+ *
+ * out[n,q,h,:] = sum_k softmax_k(scale*((q+u).k_k + (q+v).p[T-1-q+k])) v_k over keys
+ * k < valid_lengths[n]; rows of an utterance with valid_lengths[n] <= 0 are zero.
+ * scale must be finite, > 0, and scale*log2(e) finite.
+ * -------------------------------------------------------------------------------- */
+FGA_API int32_t fga_parakeet_relative_attention_check(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs, const fga_tensor_desc* output_descs, int32_t nb_outputs, float scale);
+FGA_API size_t fga_parakeet_relative_attention_workspace_size(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs);
+FGA_API int32_t fga_parakeet_relative_attention_enqueue(const fga_tensor_desc* input_descs,
+    const fga_tensor_desc* output_descs, const void* const* inputs, void* const* outputs,
+    float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------------
+ * zipformer_relative_attention (relative-position attention weights)
+ *
+ * Replaces RelativeAttentionPlugin::enqueue and enqueueRelativeAttention,
+ *   src/fast_gpu_asr/tensorrt_plugins/zipformer_relative_attention_plugin.cu:761-815
+ *   and :490-566, with the shape contract of haveValidShapes (:96-133).
+ *
+ * inputs[0] projection [N, T, H*(2*qd+4)] f32|f16|bf16 (Q heads, K heads, 4-dim pos queries)
+ * inputs[1] position   [1, 2T-1, H, 4]     same type
+ * inputs[2] mask       [N, T]              bool, True = padded key (contiguous suffix)
+ * outputs[0] weights   [N, H, T, T]        same type
+ *
+ * No scale is applied. Masked keys get weight 0, a row whose keys are all masked is
+ * zero, and query rows q >= 7 with mask[q-7] set (the 7-frame padded-query halo) are
+ * zero.
+ * -------------------------------------------------------------------------------- */
+FGA_API int32_t fga_zipformer_relative_attention_check(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs, const fga_tensor_desc* output_descs, int32_t nb_outputs);
+FGA_API size_t fga_zipformer_relative_attention_workspace_size(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs);
+FGA_API int32_t fga_zipformer_relative_attention_enqueue(const fga_tensor_desc* input_descs,
+    const fga_tensor_desc* output_descs, const void* const* inputs, void* const* outputs,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------------
+ * zipformer_attention_value (apply shared attention weights to NTC values)
+ *
+ * Replaces AttentionValuePlugin::enqueue,
+ *   src/fast_gpu_asr/tensorrt_plugins/zipformer_attention_value_plugin.cu:438-572,
+ * with the shape contract of haveValidShapes (:79-94) and field `num_heads` (:616-655).
+ *
+ * inputs[0] attention [N, Ha, T, T] f32|f16|bf16
+ * inputs[1] value     [N, T, C]     same type, C % num_heads == 0
+ * outputs[0] output   [N, T, C]     same type
+ *
+ * out[n,q,h,d] = sum_k attention[n,h,q,k] * value[n,k,h,d], fp32 accumulation.
+ * num_heads == 1 (NonlinAttention) uses attention head 0 of any Ha >= 1;
+ * num_heads > 1 requires Ha == num_heads.
+ * -------------------------------------------------------------------------------- */
+FGA_API int32_t fga_zipformer_attention_value_check(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs, const fga_tensor_desc* output_descs, int32_t nb_outputs,
+    int32_t num_heads);
+FGA_API size_t fga_zipformer_attention_value_workspace_size(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs, int32_t num_heads);
+FGA_API int32_t fga_zipformer_attention_value_enqueue(const fga_tensor_desc* input_descs,
+    const fga_tensor_desc* output_descs, const void* const* inputs, void* const* outputs,
+    int32_t num_heads, void* workspace, size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------------
+ * Library identity and diagnostics (no counterpart needed in the reference; the
+ * reference reports failures only through enqueue's return value).
+ * -------------------------------------------------------------------------------- */
+FGA_API int32_t fga_abi_version(void);
+FGA_API const char* fga_status_string(int32_t status);
+/* Name of the kernel variant the last successful enqueue on this host thread chose
+ * ("tcgen05", "simt", ...); for tests and benchmarks. */
+FGA_API const char* fga_last_kernel_variant(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FGA_ATTENTION_H */

@@ -1,0 +1,230 @@
+"""Shared parity cases: seeded inputs and hand-computed known answers.
+
+The hand-computed cases restate (in this project's own code) the known-answer
+scenarios of the reference's plugin tests:
+
+* ``tests/plugins/test_parakeet_relative_attention_plugin.py``: relative shift (:1038),
+  score promotion (:880), content attention with bias (:997), head/value layout (:1018),
+  padded keys ignored (:1025), last-key dispatch (:818), extreme logits (:910),
+  non-finite scores (:930), finite scaled logits (:960).
+* ``tests/plugins/test_zipformer_relative_attention_plugin.py``: old-sentinel masking
+  (:473), relative offset (:530), kernel-boundary key (:561), uniform masks (:616).
+* ``tests/plugins/test_zipformer_attention_value_plugin.py``: fp32 accumulation (:460),
+  unused heads ignored (:476), head/layout preservation (:441).
+
+Inputs are float32 numpy arrays holding values exactly representable in the case's
+dtype; the oracle and the CUDA path both round them to that dtype.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+PARAKEET_TOL = {"float32": 1e-4, "float16": 2e-2, "bfloat16": 2e-2}
+# Softmax-weight tolerance (max-abs). bf16 weights in [0.5, 1] are quantised in steps of
+# 2^-8 = 3.9e-3, so a one-ulp rounding difference is allowed there.
+WEIGHT_ATOL = {"float32": 1e-4, "float16": 1e-3, "bfloat16": 1e-3}
+WEIGHT_RTOL = {"float32": 0.0, "float16": 0.0, "bfloat16": 2.0**-8}
+VALUE_TOL = {"float32": 1e-4, "float16": 2e-3, "bfloat16": 1e-2}
+
+
+def quantize(x: np.ndarray, dtype: str) -> np.ndarray:
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    return t.to(getattr(torch, dtype)).float().numpy()
+
+
+# ---- Parakeet -----------------------------------------------------------------------
+def parakeet_inputs(batch, length, heads, head_dim, lengths, seed=None, sigma=0.2):
+    """N(0, sigma) projections as in the reference's plugin test generator."""
+    if seed is None:
+        seed = 20260819 + 100 * batch + length
+    rng = np.random.default_rng(seed)
+    c = heads * head_dim
+    return dict(
+        qkv=rng.normal(0.0, sigma, (batch, length, 3 * c)).astype(np.float32),
+        position=rng.normal(0.0, sigma, (1, 2 * length - 1, c)).astype(np.float32),
+        content_bias=rng.normal(0.0, sigma, (heads, head_dim)).astype(np.float32),
+        position_bias=rng.normal(0.0, sigma, (heads, head_dim)).astype(np.float32),
+        valid_lengths=np.asarray(lengths, dtype=np.int32),
+    )
+
+
+def parakeet_zero_inputs(length, heads, head_dim, valid):
+    c = heads * head_dim
+    return dict(
+        qkv=np.zeros((1, length, 3 * c), np.float32),
+        position=np.zeros((1, 2 * length - 1, c), np.float32),
+        content_bias=np.zeros((heads, head_dim), np.float32),
+        position_bias=np.zeros((heads, head_dim), np.float32),
+        valid_lengths=np.asarray([valid], np.int32),
+    )
+
+
+def parakeet_known_answers(heads=2, head_dim=64):
+    """(name, inputs, scale, expected [N,T,C] or None) for hand-computed cases."""
+    c = heads * head_dim
+    scale = head_dim**-0.5
+    cases = []
+
+    # Relative shift: row q picks position T-1-q+k; rows 1 and 4 are hot, so the three
+    # queries attend to keys 2, 0 and 1 (values 3, 1, 2).
+    x = parakeet_zero_inputs(3, heads, head_dim, 3)
+    x["qkv"][0, :, 2 * c :] = np.arange(1, 4, dtype=np.float32)[:, None]
+    x["position"].fill(-50.0)
+    x["position"][0, (1, 4), ::head_dim] = 50.0
+    x["position_bias"][:, 0] = 1.0
+    exp = np.broadcast_to(np.array((3.0, 1.0, 2.0), np.float32)[None, :, None], (1, 3, c))
+    cases.append(("relative-shift", x, scale, exp.copy()))
+
+    # Content attention with the content bias: query frames 0,1 select keys 0,1; the
+    # bias on channel 2 makes frame 2 select key 2.
+    x = parakeet_zero_inputs(3, heads, head_dim, 3)
+    q, k, v = np.split(x["qkv"], 3, axis=2)
+    v[0] = np.arange(1, 4, dtype=np.float32)[:, None]
+    for f in range(3):
+        if f < 2:
+            q[0, f, f::head_dim] = 10.0
+        k[0, f, f::head_dim] = 20.0
+    x["content_bias"][:, 2] = 5.0
+    exp = np.broadcast_to(np.arange(1, 4, dtype=np.float32)[None, :, None], (1, 3, c))
+    cases.append(("content-and-bias", x, scale, exp.copy()))
+
+    # Head and value layout: uniform attention over 4 valid keys of value f + 10*h.
+    x = parakeet_zero_inputs(7, heads, head_dim, 4)
+    x["qkv"][0, :, 2 * c :] = np.arange(7)[:, None] + np.repeat(np.arange(heads) * 10, head_dim)
+    exp = np.broadcast_to(np.repeat(np.arange(heads) * 10 + 1.5, head_dim), (1, 7, c))
+    cases.append(("head-value-layout", x, scale, exp.astype(np.float32).copy()))
+
+    # Last key dominates (exercises the final key tile at several lengths).
+    for t in (1, 31, 33, 129, 200, 257):
+        x = parakeet_zero_inputs(t, heads, head_dim, t)
+        q, k, v = np.split(x["qkv"], 3, axis=2)
+        q[0, :, ::head_dim] = 20.0
+        k[0, t - 1, ::head_dim] = 20.0
+        v[0, t - 1] = 1.0
+        cases.append((f"last-key-t{t}", x, scale, np.ones((1, t, c), np.float32)))
+
+    # Extreme but finite valid logit with one valid key: weight 1.
+    x = parakeet_zero_inputs(2, heads, head_dim, 1)
+    q, k, v = np.split(x["qkv"], 3, axis=2)
+    q[0, :, ::head_dim] = 1.0
+    k[0, 0, ::head_dim] = -1200.0 / scale
+    v[0, 0] = 1.0
+    cases.append(("extreme-valid-logit", x, scale, np.ones((1, 2, c), np.float32)))
+
+    # Zero valid length: zero rows.
+    x = parakeet_zero_inputs(5, heads, head_dim, 0)
+    x["qkv"][...] = 1.0
+    cases.append(("zero-length", x, scale, np.zeros((1, 5, c), np.float32)))
+    return cases
+
+
+def parakeet_score_promotion(dtype: str):
+    """Reference :880. H=1, D=2, scale 8: content 1.5 plus positional +-delta must be
+    summed in fp32 (not in the storage dtype) before softmax."""
+    delta = {"float16": 4e-4, "bfloat16": 3e-3}[dtype]
+    x = parakeet_zero_inputs(2, 1, 2, 2)
+    _, k, v = np.split(x["qkv"], 3, axis=2)
+    k[0, :, 1] = 1.0
+    v[0, 1, 0] = 1.0
+    x["position"][0, 1, 0] = delta
+    x["position"][0, 2, 0] = -delta
+    x["content_bias"][0] = (0.0, 1.5)
+    x["position_bias"][0] = (1.0, 0.0)
+    pos = quantize(x["position"][0, 1:, 0], dtype)
+    logits = (np.float32(1.5) + pos) * np.float32(8.0)
+    e = np.exp(logits - logits.max())
+    promoted = quantize(np.array([e[1] / e.sum()], np.float32), dtype)[0]
+    return x, 8.0, promoted
+
+
+# ---- Zipformer weights ----------------------------------------------------------------
+def zipformer_inputs(batch, length, heads=4, qd=32, seed=None, lengths=None, sigma=0.25):
+    """N(0, 0.25) projections; default lengths max(1, T-9-3b) as in the reference tests."""
+    if seed is None:
+        seed = 1000 + 100 * batch + length
+    rng = np.random.default_rng(seed)
+    pdim = heads * (2 * qd + 4)
+    projection = rng.normal(0.0, sigma, (batch, length, pdim)).astype(np.float32)
+    position = rng.normal(0.0, sigma, (1, 2 * length - 1, heads, 4)).astype(np.float32)
+    if lengths is None:
+        lengths = [max(1, length - 9 - 3 * b) for b in range(batch)]
+    mask = np.arange(length)[None, :] >= np.asarray(lengths)[:, None]
+    return dict(projection=projection, position=position, mask=mask)
+
+
+def zipformer_known_answers(heads=4, qd=32):
+    """(name, inputs, expected weights [N,H,T,T] or None)."""
+    pdim = heads * (2 * qd + 4)
+    cd = heads * qd
+    cases = []
+    # Masked keys excluded even when the valid score is far below any finite sentinel.
+    proj = np.zeros((1, 2, pdim), np.float32)
+    proj[:, :, :cd] = 50.0
+    proj[:, 0, cd : 2 * cd] = -40.0
+    pos = np.zeros((1, 3, heads, 4), np.float32)
+    mask = np.array([[False, True]])
+    exp = np.zeros((1, heads, 2, 2), np.float32)
+    exp[..., 0] = 1.0
+    cases.append(("below-old-sentinel", dict(projection=proj, position=pos, mask=mask), exp))
+
+    # Relative offset 2: query q attends to key q+2 (rows q < T-2).
+    t, off = 17, 2
+    proj = np.zeros((1, t, pdim), np.float32)
+    proj[..., 2 * cd :: 4] = 20.0
+    pos = np.zeros((1, 2 * t - 1, heads, 4), np.float32)
+    pos[:, t - 1 + off, :, 0] = 20.0
+    mask = np.zeros((1, t), bool)
+    cases.append(("relative-offset", dict(projection=proj, position=pos, mask=mask), None))
+
+    # The last key wins at lengths around tile and warp boundaries.
+    for t in (1, 7, 8, 33, 127, 128, 129, 255, 257, 385):
+        proj = np.zeros((1, t, pdim), np.float32)
+        proj[..., :cd:qd] = 20.0
+        proj[:, -1, cd : 2 * cd : qd] = 20.0
+        pos = np.zeros((1, 2 * t - 1, heads, 4), np.float32)
+        mask = np.zeros((1, t), bool)
+        exp = np.zeros((1, heads, t, t), np.float32)
+        exp[..., t - 1] = 1.0
+        cases.append((f"last-key-t{t}", dict(projection=proj, position=pos, mask=mask), exp))
+
+    # Fully padded utterance: every row is zero.
+    x = zipformer_inputs(1, 65)
+    x["mask"][:] = True
+    cases.append(("all-masked", x, np.zeros((1, heads, 65, 65), np.float32)))
+    return cases
+
+
+def check_zipformer_structure(weights: np.ndarray, mask: np.ndarray) -> None:
+    """Masked keys are zero, rows past valid+7 are zero, live rows sum to 1."""
+    for b, m in enumerate(mask):
+        valid = int(np.count_nonzero(~m))
+        live = min(weights.shape[2], valid + 7)
+        assert np.count_nonzero(weights[b][..., m]) == 0
+        assert np.count_nonzero(weights[b, :, live:]) == 0
+        if valid:
+            np.testing.assert_allclose(weights[b, :, :live].sum(axis=2), 1, rtol=5e-3, atol=5e-3)
+
+
+# ---- Zipformer attention-value ---------------------------------------------------------
+VALUE_LAYERS = (
+    # (name, attention heads, value heads, channels)
+    ("self", 4, 4, 48),
+    ("self_8_heads", 8, 8, 96),
+    ("nonlinear", 4, 1, 64),
+    ("nonlinear_8_heads", 8, 1, 64),
+    ("general_multihead", 2, 2, 10),
+    ("nonlinear_wide", 4, 1, 288),
+)
+
+
+def value_inputs(batch, length, att_heads, channels, seed):
+    rng = np.random.default_rng(seed)
+    logits = rng.normal(size=(batch, att_heads, length, length)).astype(np.float32)
+    logits -= logits.max(axis=3, keepdims=True)
+    a = np.exp(logits)
+    a /= a.sum(axis=3, keepdims=True)
+    v = rng.normal(0.0, 0.5, (batch, length, channels)).astype(np.float32)
+    return a.astype(np.float32), v

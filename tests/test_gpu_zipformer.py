@@ -1,0 +1,266 @@
+"""Zipformer relative-attention weights and attention-value: CUDA path (through the
+C ABI) vs the CPU oracle.
+
+Cases restate the reference plugin test matrices
+(``tests/plugins/test_zipformer_relative_attention_plugin.py:29-30, 473-760`` and
+``tests/plugins/test_zipformer_attention_value_plugin.py:77-83, 425-584``).
+Tolerances (max-abs): weights fp32 1e-4, fp16/bf16 1e-3 (bf16 additionally one
+storage ulp, 2^-8 relative, for weights >= 0.5); attention-value fp32 1e-4, fp16 2e-3,
+bf16 1e-2.
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from fast_gpu_asr_b200 import _lib
+from fast_gpu_asr_b200.attention import zipformer_attention_value, zipformer_relative_attention
+from oracle import zipformer_attention_value as oracle_value
+from oracle import zipformer_relative_attention as oracle_weights
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = ("float32", "float16", "bfloat16")
+BOUNDARIES = (127, 128, 129, 384, 385, 512, 513, 750, 1025)
+
+
+def weights_on_gpu(x: dict, dtype: str) -> np.ndarray:
+    dt = getattr(torch, dtype)
+    proj = torch.from_numpy(x["projection"]).to("cuda", dt)
+    pos = torch.from_numpy(x["position"]).to("cuda", dt)
+    mask = torch.from_numpy(np.asarray(x["mask"], bool)).cuda()
+    n, t = proj.shape[:2]
+    out = torch.full((n, pos.shape[2], t, t), float("nan"), dtype=dt, device="cuda")
+    zipformer_relative_attention(proj, pos, mask, out=out)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+def assert_weights_match(x, dtype, actual=None):
+    if actual is None:
+        actual = weights_on_gpu(x, dtype)
+    expected = oracle_weights(x["projection"], x["position"], x["mask"], dtype)
+    assert np.isfinite(actual).all() and (actual >= 0).all()
+    np.testing.assert_allclose(actual, expected, rtol=cases.WEIGHT_RTOL[dtype],
+                               atol=cases.WEIGHT_ATOL[dtype])
+    cases.check_zipformer_structure(actual, np.asarray(x["mask"], bool))
+    return actual
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch,length", [(1, 1), (1, 7), (2, 65), (3, 100)])
+def test_weights_match_oracle(dtype, batch, length):
+    assert_weights_match(cases.zipformer_inputs(batch, length), dtype)
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("length", BOUNDARIES)
+def test_weights_tile_and_row_boundaries(dtype, length):
+    assert_weights_match(cases.zipformer_inputs(1, length), dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("heads,qd", [(1, 1), (3, 5), (8, 32), (4, 16)])
+def test_weights_head_layouts(dtype, heads, qd):
+    assert_weights_match(cases.zipformer_inputs(2, 17, heads, qd), dtype)
+    assert_weights_match(cases.zipformer_inputs(2, 130, heads, qd), dtype)
+
+
+@pytest.mark.parametrize("path", sorted(Path(__file__).parent.joinpath("golden").glob(
+    "zipformer_*.npz")), ids=lambda p: p.stem)
+def test_weights_and_values_match_reference_golden_vectors(path):
+    g = np.load(path)
+    dt = str(g["dtype"])
+    actual = weights_on_gpu(dict(projection=g["projection"], position=g["position"],
+                                 mask=g["mask"]), dt)
+    np.testing.assert_allclose(actual, g["weights"], rtol=cases.WEIGHT_RTOL[dt],
+                               atol=cases.WEIGHT_ATOL[dt])
+    heads = int(g["num_heads"])
+    for value, out, vh in (("value_a", "out_a", heads), ("value_b", "out_b", heads),
+                           ("nonlin_value", "nonlin_out", 1)):
+        got = value_on_gpu(g["weights"], g[value], vh, dt)
+        tol = cases.VALUE_TOL[dt]
+        np.testing.assert_allclose(got, g[out], rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("name,x,expected", cases.zipformer_known_answers(),
+                         ids=[c[0] for c in cases.zipformer_known_answers()])
+def test_weights_known_answers(dtype, name, x, expected):
+    actual = weights_on_gpu(x, dtype)
+    if expected is not None:
+        np.testing.assert_array_equal(actual, expected)
+    assert_weights_match(x, dtype, actual)
+
+
+@pytest.mark.parametrize("length,padded", [(385, False), (65, True), (1025, True)])
+def test_weights_uniform_masks(length, padded):
+    x = cases.zipformer_inputs(1, length)
+    x["mask"][:] = padded
+    for dtype in ("float16", "bfloat16"):
+        assert_weights_match(x, dtype)
+
+
+@pytest.mark.parametrize("length", [65, 385, 1025])
+def test_weights_contain_nonfinite_padding(length):
+    """NaN in padded keys and in halo-zeroed query rows never reaches the output."""
+    x = cases.zipformer_inputs(1, length)
+    cd = 4 * 32
+    m = x["mask"][0]
+    x["projection"][0, m, cd : 2 * cd] = np.nan
+    qmask = np.zeros(length, bool)
+    qmask[7:] = m[: length - 7]
+    x["projection"][0, qmask] = np.nan
+    for dtype in DTYPES:
+        assert_weights_match(x, dtype)
+
+
+def test_weights_large_constant_logits():
+    """Equal large logits normalise to exactly uniform rows (no overflow)."""
+    for dtype, (qv, pv) in (("float16", (132, 252)), ("bfloat16", (144, 248))):
+        x = cases.zipformer_inputs(1, 1025)
+        x["projection"].fill(0)
+        x["position"].fill(0)
+        x["mask"][:] = False
+        x["projection"][..., 2 * 128 :: 4] = qv
+        x["position"][..., 0] = pv
+        w = weights_on_gpu(x, dtype)
+        assert np.isfinite(w).all()
+        np.testing.assert_allclose(w, 1 / 1025, rtol=5e-3, atol=0)
+
+
+def test_weights_guard_bands_and_graph_replay():
+    x = cases.zipformer_inputs(2, 200)
+    proj = torch.from_numpy(x["projection"]).to("cuda", torch.bfloat16)
+    pos = torch.from_numpy(x["position"]).to("cuda", torch.bfloat16)
+    mask = torch.from_numpy(x["mask"]).cuda()
+    n_out = 2 * 4 * 200 * 200
+    store = torch.full((n_out + 256,), 7, dtype=torch.bfloat16, device="cuda")
+    out = store[128 : 128 + n_out].view(2, 4, 200, 200)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        zipformer_relative_attention(proj, pos, mask, out=out, stream=s)
+    s.synchronize()
+    assert (store[:128] == 7).all() and (store[128 + n_out :] == 7).all()
+    first = assert_weights_match(x, "bfloat16", out.float().cpu().numpy())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        zipformer_relative_attention(proj, pos, mask, out=out, stream=s)
+    for _ in range(2):
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.float().cpu().numpy(), first)
+
+
+def test_weights_full_size_stack1_properties():
+    """Config 3 stack 1 at full size (256 x 750, 4 heads, bf16): structure holds for every
+    utterance and sampled utterances match the oracle."""
+    from fast_gpu_asr_b200.workloads import (make_zipformer_layer, zipformer_input_lengths,
+                                             zipformer_stack_lengths)
+
+    lengths = zipformer_stack_lengths(zipformer_input_lengths(256, seed=1), 1)
+    layer = make_zipformer_layer(256, 750, 192, 4, torch.bfloat16, "cuda", 5, lengths)
+    w = zipformer_relative_attention(layer.projection, layer.position, layer.mask)
+    torch.cuda.synchronize()
+    assert torch.isfinite(w).all()
+    sums = w.float().sum(dim=3)  # [N, H, T]
+    t = torch.arange(750, device="cuda")
+    live = t[None, :] < (torch.as_tensor(lengths, device="cuda")[:, None] + 7)
+    assert torch.allclose(sums[live[:, None, :].expand_as(sums)], torch.ones(()), atol=2e-2)
+    assert (sums[~live[:, None, :].expand_as(sums)] == 0).all()
+    for b in (0, 128, 255):
+        x = dict(projection=layer.projection[b : b + 1].float().cpu().numpy(),
+                 position=layer.position.float().cpu().numpy(),
+                 mask=layer.mask[b : b + 1].cpu().numpy())
+        assert_weights_match(x, "bfloat16", w[b : b + 1].float().cpu().numpy())
+
+
+# ---- attention-value ------------------------------------------------------------------
+def value_on_gpu(a: np.ndarray, v: np.ndarray, heads: int, dtype: str) -> np.ndarray:
+    dt = getattr(torch, dtype)
+    at = torch.from_numpy(np.ascontiguousarray(a)).to("cuda", dt)
+    vt = torch.from_numpy(np.ascontiguousarray(v)).to("cuda", dt)
+    out = torch.full_like(vt, float("nan"))
+    zipformer_attention_value(at, vt, heads, out=out)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("layer", cases.VALUE_LAYERS, ids=[c[0] for c in cases.VALUE_LAYERS])
+@pytest.mark.parametrize("batch,length", [(1, 1), (1, 3), (2, 17), (2, 32), (2, 33), (3, 65),
+                                          (2, 129), (1, 300)])
+def test_value_matches_oracle(dtype, layer, batch, length):
+    name, ah, vh, ch = layer
+    a, v = cases.value_inputs(batch, length, ah, ch, seed=1000 + 100 * batch + length)
+    got = value_on_gpu(a, v, vh, dtype)
+    expected = oracle_value(a, v, vh, dtype)
+    assert np.isfinite(got).all()
+    tol = cases.VALUE_TOL[dtype]
+    np.testing.assert_allclose(got, expected, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_value_accumulates_in_fp32(dtype):
+    for name, ah, vh, ch in cases.VALUE_LAYERS:
+        a = np.ones((1, ah, 4, 4), np.float32)
+        v = np.broadcast_to(np.array((2048.0, 1.0, 1.0, -2048.0), np.float32).reshape(1, 4, 1),
+                            (1, 4, ch)).copy()
+        np.testing.assert_array_equal(value_on_gpu(a, v, vh, dtype), 2.0)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_value_preserves_query_key_and_head_layout(dtype):
+    coeff = np.array((0.0, 0.5, -1.0, 2.0), np.float32)
+    for name, ah, vh, ch in cases.VALUE_LAYERS:
+        a = np.zeros((2, ah, 3, 3), np.float32)
+        b, h, q = np.indices((2, ah, 3))
+        k = (2 * q + h + b) % 3
+        a[b, h, q, k] = coeff[(q + 2 * h + 3 * b) % 4]
+        b, kk, c = np.indices((2, 3, ch))
+        v = ((7 * b + 3 * kk + c) % 23 - 11).astype(np.float32)
+        np.testing.assert_array_equal(value_on_gpu(a, v, vh, dtype), oracle_value(a, v, vh, dtype))
+
+
+def test_value_ignores_unused_attention_heads():
+    for name, ah, vh, ch in cases.VALUE_LAYERS:
+        if vh != 1:
+            continue
+        a, v = cases.value_inputs(2, 32, ah, ch, seed=2027)
+        a[:, 1:] = np.nan
+        for dtype in DTYPES:
+            got = value_on_gpu(a, v, 1, dtype)
+            assert np.isfinite(got).all()
+            np.testing.assert_allclose(got, oracle_value(a, v, 1, dtype), rtol=1e-2, atol=1e-2)
+
+
+def test_value_full_size_stack1_linearity():
+    """Config 3 stack 1 (256 x 750, bf16): exact linearity in V and sampled oracle rows."""
+    from fast_gpu_asr_b200.workloads import (make_zipformer_layer, zipformer_input_lengths,
+                                             zipformer_stack_lengths)
+
+    lengths = zipformer_stack_lengths(zipformer_input_lengths(256, seed=1), 1)
+    layer = make_zipformer_layer(256, 750, 192, 4, torch.bfloat16, "cuda", 5, lengths)
+    w = zipformer_relative_attention(layer.projection, layer.position, layer.mask)
+    for value, heads in ((layer.value_a, 4), (layer.nonlin_value, 1)):
+        o1 = zipformer_attention_value(w, value, heads)
+        o2 = zipformer_attention_value(w, value * 2, heads)
+        torch.cuda.synchronize()
+        assert torch.equal(o2, o1 * 2)
+        for b in (0, 255):
+            exp = oracle_value(w[b : b + 1].float().cpu().numpy(),
+                               value[b : b + 1].float().cpu().numpy(), heads, "bfloat16")
+            np.testing.assert_allclose(o1[b : b + 1].float().cpu().numpy(), exp, rtol=1e-2,
+                                       atol=1e-2)
+
+
+def test_variant_reported():
+    a, v = cases.value_inputs(1, 33, 4, 48, seed=1)
+    value_on_gpu(a, v, 4, "bfloat16")
+    assert _lib.last_kernel_variant() in ("tcgen05", "simt")
