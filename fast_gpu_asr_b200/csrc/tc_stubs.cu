@@ -2,7 +2,6 @@
 #include "fga_kernels.h"
 
 namespace fga {
-cudaError_t launch_parakeet_tc(const ParakeetProblem&, cudaStream_t) { return cudaErrorNotSupported; }
 cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem&, cudaStream_t) {
     return cudaErrorNotSupported;
 }
