@@ -1,42 +1,50 @@
 // Parakeet relative-position MHSA on 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// Work item = one 128-query tile of one (utterance n, head h), head_dim D = 128. For
-// each 128-key tile j of the utterance's valid keys:
+// Work item = one 128-query tile (rows q0..q0+127) of one (utterance n, head h), head
+// dim D = 128. Keys are visited in tiles of 128 (k0 = 128 j) up to the valid length.
 //
-//   S_c  = (Q+u) K_j^T                128 x 128   tcgen05.mma -> TMEM cols [0,128)
-//   S_b  = (Q+v) Pband_j^T            128 x 256   tcgen05.mma -> TMEM cols [128,384)
-//   logit(q,k) = scale * (S_c[q,k] + S_b[q, 127 - q + k])      (Transformer-XL shift)
+//   S_c(j) = (Q+u) K_j^T      128 x 128   tcgen05.mma -> TMEM cols [0,128)
+//   band   = (Q+v) Pband^T                 tcgen05.mma -> TMEM band ring
+//   logit(q,k) = scale * (S_c[q,k] + band[q, T-1-q+k])     (Transformer-XL shift)
 //   online softmax over keys k < valid_length (fp32, base 2)
-//   O   += P_j V_j                    128 x 128   tcgen05.mma -> TMEM cols [384,512)
+//   O     += P_j V_j          128 x 128   tcgen05.mma -> TMEM cols [384,512)
 //
-// Pband_j holds the 256 rows of the positional projection that the tile's (q, k) pairs
-// touch: relative index T-1-q+k ranges over [T-128-q0+k0, T-1-q0+k0+127], so row i of
-// S_b needs columns 127-i .. 255-i. A warp loads the 64-column window its 32 rows span
-// and every thread shifts its own row into place with a 5-stage predicated barrel shift.
+// Positional band. Key tile j touches relative rows r0 + 128 j + [0, 256) with
+// r0 = T-128-q0; row i of the tile needs band column 127-i+kk for key kk. The 256
+// columns of tile j are two 128-row "halves" m = j and m = j+1 of the item's band
+// (half m = positional rows r0 + 128 m + [0,128)), and tile j+1 reuses half j+1. So each
+// half is computed once, by an N=128 MMA into a two-slot TMEM ring (slot m % 2):
+// halves 0 and 1 together with S_c(0), half j+2 together with S_c(j+1). The score MMAs
+// then do exactly the algorithmic work (no band recomputation).
+//
+// Skew. A warp loads the 64-column window its 32 rows span (two 32-column pieces, each
+// inside one half) and every thread shifts its own row into place with a 5-stage
+// predicated barrel shift.
 //
 // CTA organisation (persistent: one CTA per SM walks the work items):
-//   warps 0-7  softmax. Warp w owns TMEM lanes 32*(w%4).. (rows) and key half w/4
-//              (64 keys of each tile); the two warps of a row group exchange the row
-//              max through shared memory behind a 64-thread named barrier.
-//   warp 8     TMA producer: lane 0 loads Q and K + positional band, lane 1 loads V.
+//   warps 0-7  softmax. Warp w owns TMEM lanes 32*(w%4).. (rows) and key half w/4 (64
+//              keys of each tile); the two warps of a row group exchange the row max
+//              through shared memory behind a 64-thread named barrier. After reading the
+//              scores of an item's last tile they form the next item's biased queries,
+//              so the next item's first MMAs overlap this item's exponentials and
+//              epilogue.
+//   warp 8     TMA producer: lane 0 loads Q, K and positional chunks, lane 1 loads V.
 //   warp 9     MMA issuer (one thread) and TMEM owner.
-// The next tile's score MMAs are issued as soon as the softmax warps have copied the
-// current scores to registers, so S(j+1) overlaps the exponentials of tile j. O is
-// rescaled only when a row max grows by more than 2^8 (the unnormalised probabilities
-// stay <= 256, exact in f16/bf16 range).
+// O is rescaled only when a row max grows by more than 2^8 (the unnormalised
+// probabilities stay <= 256, exact in f16/bf16 range).
 //
 // Reference semantics (parakeet_relative_attention_plugin.cu): biased queries are
 // formed in fp32 and rounded to the I/O dtype (:268-281); scores are summed and scaled
 // in fp32 (:503-508); only keys below the valid length contribute; valid_length <= 0
 // gives zero rows (:478-486); every query row < T is produced (:472-476). Scores stay
-// in fp32 between the two GEMMs (the reference stores them in the I/O dtype). The log2(e)
-// factor is folded into the scale, so this kernel serves scale <= 1 (every real model:
-// 1/sqrt(D)); larger scales run on the SIMT kernel, which subtracts the row max before
-// converting to base 2 exactly like the reference.
+// in fp32 between the GEMMs (the reference stores them in the I/O dtype). log2(e) is
+// folded into the scale, so this kernel serves scale <= 1 (every real model:
+// 1/sqrt(D)); larger scales run on the SIMT kernel, which subtracts the row max
+// before converting to base 2 exactly like the reference.
 //
 // Data movement: Q, K and V tiles arrive by TMA from the fused [N, T, 3C] projection
-// through a 3-D tensor map (rows past T of an utterance read as zero), the positional
-// band through a 2-D map over [2T-1, C] (rows outside the table read as zero). All
+// through a 3-D tensor map (rows past T of an utterance read as zero), positional
+// chunks through a 2-D map over [2T-1, C] (rows outside the table read as zero). All
 // operand tiles use the 128-byte-swizzled canonical UMMA layouts.
 #include <cuda.h>
 
@@ -52,40 +60,41 @@ namespace {
 using namespace sm100;
 
 constexpr int kM = 128;       // query rows per work item
-constexpr int kN = 128;       // keys per tile
+constexpr int kN = 128;       // keys per tile (= rows per positional half)
 constexpr int kD = 128;       // head dim
-constexpr int kBand = 256;    // positional rows per tile (kM + kN - 1, rounded to 256)
 constexpr int kSoftmaxWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 320;
 constexpr int kHalfKeys = kN / 2;
 
-// Shared-memory map (bytes from the 1024-aligned dynamic base).
-constexpr uint32_t kAtom = kM * 128;                 // one 64-column swizzle atom of a 128-row tile
-constexpr uint32_t kSmemQu = 0;                      // 2 atoms (TMA lands Q here first)
-constexpr uint32_t kSmemQv = kSmemQu + 2 * kAtom;    // 2 atoms
-constexpr uint32_t kSmemK = kSmemQv + 2 * kAtom;     // 2 atoms
-constexpr uint32_t kSmemV = kSmemK + 2 * kAtom;      // 2 atoms
-constexpr uint32_t kBandAtom = kBand * 128;
-constexpr uint32_t kSmemBand = kSmemV + 2 * kAtom;   // 2 atoms of 256 rows
-constexpr uint32_t kSmemP = kSmemBand + 2 * kBandAtom;  // 2 atoms
-constexpr uint32_t kSmemXchg = kSmemP + 2 * kAtom;   // [2 halves][128 rows] fp32
+// Shared-memory map (bytes from the 1024-aligned dynamic base). Every tile is
+// 128 rows x 128 channels = two 64-channel swizzle atoms of 16 KB.
+constexpr uint32_t kAtom = 128 * 128;
+constexpr uint32_t kTile = 2 * kAtom;
+constexpr uint32_t kSmemQu = 0;                 // TMA lands Q here first
+constexpr uint32_t kSmemQv = kSmemQu + kTile;
+constexpr uint32_t kSmemK = kSmemQv + kTile;
+constexpr uint32_t kSmemV = kSmemK + kTile;
+constexpr uint32_t kSmemB0 = kSmemV + kTile;    // positional chunk slots 0 and 1
+constexpr uint32_t kSmemP = kSmemB0 + 2 * kTile;
+constexpr uint32_t kSmemXchg = kSmemP + kTile;  // [2 halves][128 rows] fp32
 constexpr uint32_t kSmemBar = kSmemXchg + 2 * kM * 4;
-constexpr uint32_t kNumBars = 13;
+constexpr uint32_t kNumBars = 17;
 constexpr uint32_t kSmemBytes = kSmemBar + kNumBars * 8 + 16;
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColSc = 0, kColSb = 128, kColO = 384;
+constexpr uint32_t kColSc = 0, kColBand = 128, kColO = 384;  // band ring: 2 x 128 cols
 
-constexpr uint32_t kKBandTxBytes = 2 * kAtom + 2 * kBandAtom;
-constexpr uint32_t kVTxBytes = 2 * kAtom;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 enum : uint32_t {
-    kBarQFull = 0, kBarQReady, kBarQEmpty, kBarKBFull, kBarKBEmpty, kBarVFull, kBarVEmpty,
-    kBarSFull, kBarSFree, kBarPFull, kBarODone, kBarOFree, kBarDrain
+    kBarQFull = 0, kBarQReady, kBarQEmpty, kBarKFull, kBarKEmpty, kBarVFull, kBarVEmpty,
+    kBarSFull, kBarSFree, kBarPFull, kBarODone, kBarOFree, kBarDrain,
+    kBarBFull0, kBarBFull1,  // positional chunk slot s full: kBarBFull0 + s
+    kBarBEmpty0              // slot s empty: kBarBEmpty0 + s (entries 15 and 16)
 };
+static_assert(kBarBEmpty0 + 2 == kNumBars, "barrier table");
 
 __device__ unsigned int g_parakeet_tc_error = 0;
 
@@ -122,7 +131,7 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
 }
 
 // out[j] = v[j + s] for j < 32, s in [0, 31]: five predicated stages (16, 8, 4, 2, 1).
-__device__ __forceinline__ void barrel_shift(float (&v)[64], uint32_t s) {
+__device__ __forceinline__ void barrel_shift(uint32_t (&v)[64], uint32_t s) {
 #pragma unroll
     for (int j = 0; j < 47; ++j) v[j] = (s & 16u) ? v[j + 16] : v[j];
 #pragma unroll
@@ -133,6 +142,16 @@ __device__ __forceinline__ void barrel_shift(float (&v)[64], uint32_t s) {
     for (int j = 0; j < 33; ++j) v[j] = (s & 2u) ? v[j + 2] : v[j];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = (s & 1u) ? v[j + 1] : v[j];
+}
+
+template <int N> __device__ __forceinline__ float tree_max(const float (&x)[N]) {
+    float m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = x[i];
+#pragma unroll
+    for (int i = 8; i < N; ++i) m[i & 7] = fmaxf(m[i & 7], x[i]);
+    return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])),
+                 fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
 struct Item {
@@ -178,34 +197,73 @@ struct Sync {
     }
 };
 
+// TMEM column of virtual band column x (0..255) of a tile whose lower half lives in
+// ring slot `slot_lo` (the upper half is in the other slot).
+__device__ __forceinline__ uint32_t band_col(uint32_t x, uint32_t slot_lo) {
+    const uint32_t slot = (x < 128u) ? slot_lo : (slot_lo ^ 1u);
+    return kColBand + slot * 128u + (x & 127u);
+}
+
 // Scaled base-2 logits of this thread's 64 keys of the tile (two 32-key chunks).
 template <bool kMasked>
 __device__ __forceinline__ void load_logits(float (&s)[kHalfKeys], uint32_t tmem_row,
                                             int group, int half, uint32_t shift,
-                                            float scale_log2, int nvalid) {
+                                            uint32_t slot_lo, float scale_log2, int nvalid) {
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
         const int c = 2 * half + cc;  // 32-key chunk of the tile
-        uint32_t sc[32], b0[32], b1[32];
-        const uint32_t base = 96u - 32u * group + 32u * c;
+        uint32_t sc[32], band[64];
+        const uint32_t base = 96u - 32u * group + 32u * c;  // band window [base, base+64)
         tmem_ld32(tmem_row + kColSc + c * 32, sc);
-        tmem_ld32(tmem_row + kColSb + base, b0);
-        tmem_ld32(tmem_row + kColSb + base + 32, b1);
+        tmem_ld32(tmem_row + band_col(base, slot_lo), *reinterpret_cast<uint32_t(*)[32]>(band));
+        tmem_ld32(tmem_row + band_col(base + 32, slot_lo),
+                  *reinterpret_cast<uint32_t(*)[32]>(band + 32));
         tmem_wait_ld();
         reg_fence(sc);
-        reg_fence(b0);
-        reg_fence(b1);
-        float band[64];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            band[e] = __uint_as_float(b0[e]);
-            band[e + 32] = __uint_as_float(b1[e]);
-        }
+        reg_fence(band);
         barrel_shift(band, shift);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-            const float v = (__uint_as_float(sc[e]) + band[e]) * scale_log2;
+            const float v = (__uint_as_float(sc[e]) + __uint_as_float(band[e])) * scale_log2;
             s[cc * 32 + e] = (!kMasked || c * 32 + e < nvalid) ? v : -INFINITY;
+        }
+    }
+}
+
+// (Q+u), (Q+v) in fp32, rounded to T (reference .cu:268-281), for this warp's 32 rows
+// and head channels [64*half, 64*half+64). One 8-channel chunk at a time keeps few
+// registers live (this runs while the current tile's logits are held in registers);
+// the bias vectors are L1-resident after the first warp reads them.
+template <typename T>
+__device__ __forceinline__ void bias_queries(uint8_t* smem, const T* __restrict__ ub,
+                                             const T* __restrict__ vb, int row, int half) {
+#pragma unroll 1
+    for (int g4 = 0; g4 < 2; ++g4) {
+        uint4 uw4[4], vw4[4];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+            const int c = half * 8 + g4 * 4 + c4;
+            uw4[c4] = __ldg(reinterpret_cast<const uint4*>(ub + c * 8));
+            vw4[c4] = __ldg(reinterpret_cast<const uint4*>(vb + c * 8));
+        }
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+            const uint32_t off = half * kAtom + sw128_offset(row, g4 * 4 + c4);
+            const uint4 qw = *reinterpret_cast<const uint4*>(smem + kSmemQu + off);
+            const uint32_t qs[4] = {qw.x, qw.y, qw.z, qw.w};
+            const uint32_t us[4] = {uw4[c4].x, uw4[c4].y, uw4[c4].z, uw4[c4].w};
+            const uint32_t vs[4] = {vw4[c4].x, vw4[c4].y, vw4[c4].z, vw4[c4].w};
+            uint32_t a[4], b[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 q = unpack2<T>(qs[e]);
+                const float2 u = unpack2<T>(us[e]);
+                const float2 v = unpack2<T>(vs[e]);
+                a[e] = pack2<T>(q.x + u.x, q.y + u.y);
+                b[e] = pack2<T>(q.x + v.x, q.y + v.y);
+            }
+            *reinterpret_cast<uint4*>(smem + kSmemQu + off) = make_uint4(a[0], a[1], a[2], a[3]);
+            *reinterpret_cast<uint4*>(smem + kSmemQv + off) = make_uint4(b[0], b[1], b[2], b[3]);
         }
     }
 }
@@ -236,9 +294,11 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
         return;
     }
     if (tid == 0) {
-        const uint32_t counts[kNumBars] = {1, kSoftmaxWarps, 1, 1, 1, 1, 1, 1, kSoftmaxWarps,
-                                           kSoftmaxWarps, 1, kSoftmaxWarps, 1};
-        for (uint32_t i = 0; i < kNumBars; ++i) mbar_init(sync.bar(i), counts[i]);
+        for (uint32_t i = 0; i < kNumBars; ++i) {
+            const bool per_warp = i == kBarQReady || i == kBarSFree || i == kBarPFull ||
+                                  i == kBarOFree;
+            mbar_init(sync.bar(i), per_warp ? kSoftmaxWarps : 1);
+        }
         *abort_word = 0;
         fence_mbar_init();
         prefetch_tensormap(&qkv_map);
@@ -255,35 +315,77 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
     const uint32_t tmem = *tmem_slot;
 
     if (warp == kProducerWarp) {
-        // ---- TMA producer: lane 0 loads Q and K+band, lane 1 loads V ------------------------
+        // ---- TMA producer: lane 0 loads Q, K and positional chunks, lane 1 loads V ---------
         if (lane == 0) {
-            uint32_t q_iter = 0, kb_iter = 0;
+            uint32_t q_iter = 0, k_iter = 0, c_iter = 0;
             bool ok = true;
+            auto load_chunk = [&](const Item& it, int m) -> bool {
+                const uint32_t slot = c_iter & 1;
+                if (c_iter >= 2 && !sync.wait(kBarBEmpty0 + slot, ((c_iter >> 1) - 1) & 1))
+                    return false;
+                const int r = length - kM - it.q0 + m * kN;  // first positional row
+                const uint32_t b = sync.bar(kBarBFull0 + slot);
+                mbar_expect_tx(b, kTile);
+                tma_load_2d(sbase + kSmemB0 + slot * kTile, &pos_map, b, it.h * kD, r);
+                tma_load_2d(sbase + kSmemB0 + slot * kTile + kAtom, &pos_map, b,
+                            it.h * kD + 64, r);
+                ++c_iter;
+                return true;
+            };
+            auto load_k = [&](const Item& it, int j) -> bool {
+                if (k_iter > 0 && !sync.wait(kBarKEmpty, (k_iter - 1) & 1)) return false;
+                const uint32_t b = sync.bar(kBarKFull);
+                mbar_expect_tx(b, kTile);
+                tma_load_3d(sbase + kSmemK, &qkv_map, b, C + it.h * kD, j * kN, it.n);
+                tma_load_3d(sbase + kSmemK + kAtom, &qkv_map, b, C + it.h * kD + 64, j * kN,
+                            it.n);
+                ++k_iter;
+                return true;
+            };
+            // Warm L2 with everything an item will load (Q, K and V tiles, positional
+            // chunks), one item ahead, so the SMEM loads that wait for a free buffer
+            // hit L2 instead of HBM.
+            auto prefetch_item = [&](int item) {
+                if (item >= num_items) return;
+                const Item it = decode_item(item, qtiles, heads, length, lengths);
+                if (it.tiles == 0) return;
+                for (int a = 0; a < 2; ++a) {
+                    const int x = it.h * kD + 64 * a;
+                    tma_prefetch_3d(&qkv_map, x, it.q0, it.n);
+                    for (int j = 0; j < it.tiles; ++j) {
+                        tma_prefetch_3d(&qkv_map, C + x, j * kN, it.n);
+                        tma_prefetch_3d(&qkv_map, 2 * C + x, j * kN, it.n);
+                    }
+                    for (int m = 0; m <= it.tiles; ++m)
+                        tma_prefetch_2d(&pos_map, x, length - kM - it.q0 + m * kN);
+                }
+            };
+            prefetch_item(blockIdx.x);
             for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
                 const Item it = decode_item(item, qtiles, heads, length, lengths);
                 if (it.tiles == 0) continue;
+                prefetch_item(item + gridDim.x);
                 if (q_iter > 0 && !(ok = sync.wait(kBarQEmpty, (q_iter - 1) & 1))) break;
-                mbar_expect_tx(sync.bar(kBarQFull), 2 * kAtom);
+                mbar_expect_tx(sync.bar(kBarQFull), kTile);
                 tma_load_3d(sbase + kSmemQu, &qkv_map, sync.bar(kBarQFull), it.h * kD, it.q0, it.n);
                 tma_load_3d(sbase + kSmemQu + kAtom, &qkv_map, sync.bar(kBarQFull),
                             it.h * kD + 64, it.q0, it.n);
                 ++q_iter;
-                for (int j = 0; j < it.tiles; ++j) {
-                    if (kb_iter > 0 && !(ok = sync.wait(kBarKBEmpty, (kb_iter - 1) & 1))) break;
-                    const int k0 = j * kN;
-                    const int r0 = length - kM - it.q0 + k0;  // first positional row of the band
-                    const uint32_t b = sync.bar(kBarKBFull);
-                    mbar_expect_tx(b, kKBandTxBytes);
-                    tma_load_3d(sbase + kSmemK, &qkv_map, b, C + it.h * kD, k0, it.n);
-                    tma_load_3d(sbase + kSmemK + kAtom, &qkv_map, b, C + it.h * kD + 64, k0, it.n);
-                    tma_load_2d(sbase + kSmemBand, &pos_map, b, it.h * kD, r0);
-                    tma_load_2d(sbase + kSmemBand + kBandAtom, &pos_map, b, it.h * kD + 64, r0);
-                    ++kb_iter;
-                }
+                // In the order the MMA consumes them: K(0), chunk 0, chunk 1, then
+                // K(j), chunk j+1 for j >= 1.
+                if (!(ok = load_k(it, 0)) || !(ok = load_chunk(it, 0)) ||
+                    !(ok = load_chunk(it, 1)))
+                    break;
+                for (int j = 1; j < it.tiles && ok; ++j)
+                    ok = load_k(it, j) && load_chunk(it, j + 1);
             }
             if (!ok) {  // drain our own copies in flight (bounded) before teardown
                 if (q_iter) mbar_wait(sync.bar(kBarQFull), (q_iter - 1) & 1);
-                if (kb_iter) mbar_wait(sync.bar(kBarKBFull), (kb_iter - 1) & 1);
+                if (k_iter) mbar_wait(sync.bar(kBarKFull), (k_iter - 1) & 1);
+                for (uint32_t s = 0; s < 2 && s < c_iter; ++s) {
+                    const uint32_t last = c_iter - 1 - s;  // the last load into slot last&1
+                    mbar_wait(sync.bar(kBarBFull0 + (last & 1)), (last >> 1) & 1);
+                }
             }
         } else if (lane == 1) {
             uint32_t v_iter = 0;
@@ -293,7 +395,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 for (int j = 0; j < it.tiles; ++j) {
                     if (v_iter > 0 && !(ok = sync.wait(kBarVEmpty, (v_iter - 1) & 1))) break;
                     const uint32_t b = sync.bar(kBarVFull);
-                    mbar_expect_tx(b, kVTxBytes);
+                    mbar_expect_tx(b, kTile);
                     tma_load_3d(sbase + kSmemV, &qkv_map, b, 2 * C + it.h * kD, j * kN, it.n);
                     tma_load_3d(sbase + kSmemV + kAtom, &qkv_map, b, 2 * C + it.h * kD + 64,
                                 j * kN, it.n);
@@ -303,69 +405,127 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
             if (!ok && v_iter) mbar_wait(sync.bar(kBarVFull), (v_iter - 1) & 1);
         }
     } else if (warp == kMmaWarp) {
-        // ---- MMA issuer (one thread) -------------------------------------------------------
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = idesc_f16(Fmt<T>::v, kM, kN, 0, 0);
-            constexpr uint32_t idesc_b = idesc_f16(Fmt<T>::v, kM, kBand, 0, 0);
-            constexpr uint32_t idesc_o = idesc_f16(Fmt<T>::v, kM, kD, 0, 1);
-            uint32_t q_iter = 0, kb_iter = 0, v_iter = 0, s_iter = 0, items_done = 0;
-            bool ok = true;
-            auto issue_s = [&](bool last_of_item) -> bool {
-                if (!sync.wait(kBarKBFull, kb_iter & 1)) return false;
-                if (s_iter > 0 && !sync.wait(kBarSFree, (s_iter - 1) & 1)) return false;
-                tc_fence_after();
+        // ---- MMA issuer: the whole warp runs this loop (uniform control flow, warp-
+        // uniform descriptors); one elected lane issues each tcgen05 instruction. A
+        // single-thread issuer is starved of issue slots by the busy softmax warps.
+        constexpr uint32_t idesc_s = idesc_f16(Fmt<T>::v, kM, kN, 0, 0);
+        constexpr uint32_t idesc_o = idesc_f16(Fmt<T>::v, kM, kD, 0, 1);
+        // Base descriptors (K-major operands: +32 B per 16-channel K step inside an
+        // atom, +kAtom per atom; V is MN-major: +2048 B per 16-key step).
+        const uint64_t d_qu = sw128_desc(sbase + kSmemQu, 16, 1024);
+        const uint64_t d_qv = sw128_desc(sbase + kSmemQv, 16, 1024);
+        const uint64_t d_k = sw128_desc(sbase + kSmemK, 16, 1024);
+        const uint64_t d_b0 = sw128_desc(sbase + kSmemB0, 16, 1024);
+        const uint64_t d_p = sw128_desc(sbase + kSmemP, 16, 1024);
+        const uint64_t d_v = sw128_desc(sbase + kSmemV, kAtom, 1024);
+        auto kstep = [](uint32_t ks) -> uint64_t {  // descriptor offset (16-byte units)
+            return static_cast<uint64_t>(((ks >> 2) * kAtom + (ks & 3) * 32) >> 4);
+        };
+        uint32_t q_iter = 0, k_iter = 0, c_iter = 0, h_iter = 0, v_iter = 0, s_iter = 0,
+                 items_done = 0;
+        bool ok = true;
+        auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+            return __all_sync(0xffffffffu, sync.wait(bar, parity));
+        };
+        // One positional half: band ring slot (h_iter % 2) = Qv . chunk(c_iter)^T.
+        auto band_half = [&]() -> bool {
+            const uint32_t slot = c_iter & 1;
+            if (!wait(kBarBFull0 + slot, (c_iter >> 1) & 1)) return false;
+            tc_fence_after();
+            const uint32_t d = tmem + kColBand + (h_iter & 1) * 128;
+            const uint64_t b = d_b0 + ((slot * kTile) >> 4);
+            if (elect_one()) {
 #pragma unroll
-                for (int ks = 0; ks < kD / 16; ++ks) {
-                    const uint32_t a = ks >> 2, koff = (ks & 3) * 32;
-                    const uint64_t qu = sw128_desc(sbase + kSmemQu + a * kAtom + koff, 16, 1024);
-                    const uint64_t qv = sw128_desc(sbase + kSmemQv + a * kAtom + koff, 16, 1024);
-                    const uint64_t kd = sw128_desc(sbase + kSmemK + a * kAtom + koff, 16, 1024);
-                    const uint64_t bd =
-                        sw128_desc(sbase + kSmemBand + a * kBandAtom + koff, 16, 1024);
-                    umma_f16_ss(tmem + kColSc, qu, kd, idesc_s, ks > 0);
-                    umma_f16_ss(tmem + kColSb, qv, bd, idesc_b, ks > 0);
-                }
+                for (uint32_t ks = 0; ks < kD / 16; ++ks)
+                    umma_f16_ss(d, d_qv + kstep(ks), b + kstep(ks), idesc_s, ks > 0);
+                umma_commit(sync.bar(kBarBEmpty0 + slot));
+            }
+            __syncwarp();
+            ++c_iter;
+            ++h_iter;
+            return true;
+        };
+        // Score MMAs of one tile: content S_c and the new positional half(s).
+        auto issue_s = [&](bool first_of_item, bool last_of_item) -> bool {
+            if (!wait(kBarKFull, k_iter & 1)) return false;
+            if (s_iter > 0 && !wait(kBarSFree, (s_iter - 1) & 1)) return false;
+            tc_fence_after();
+            if (elect_one()) {
+#pragma unroll
+                for (uint32_t ks = 0; ks < kD / 16; ++ks)
+                    umma_f16_ss(tmem + kColSc, d_qu + kstep(ks), d_k + kstep(ks), idesc_s, ks > 0);
+                umma_commit(sync.bar(kBarKEmpty));
+            }
+            __syncwarp();
+            ++k_iter;
+            if (first_of_item && !band_half()) return false;
+            if (!band_half()) return false;
+            if (elect_one()) {
                 umma_commit(sync.bar(kBarSFull));
-                umma_commit(sync.bar(kBarKBEmpty));
                 if (last_of_item) umma_commit(sync.bar(kBarQEmpty));
-                ++kb_iter;
-                ++s_iter;
-                return true;
-            };
-            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-                const Item it = decode_item(item, qtiles, heads, length, lengths);
-                if (it.tiles == 0) continue;
-                if (!(ok = sync.wait(kBarQReady, q_iter & 1))) break;
-                ++q_iter;
-                if (!(ok = issue_s(it.tiles == 1))) break;
-                for (int j = 0; j < it.tiles && ok; ++j) {
-                    const bool more = j + 1 < it.tiles;
-                    if (more && !(ok = issue_s(j + 2 == it.tiles))) break;
-                    if (!(ok = sync.wait(kBarPFull, (s_iter - (more ? 2 : 1)) & 1))) break;
-                    if (!(ok = sync.wait(kBarVFull, v_iter & 1))) break;
-                    if (j == 0 && items_done > 0 &&
-                        !(ok = sync.wait(kBarOFree, (items_done - 1) & 1)))
-                        break;
-                    tc_fence_after();
+            }
+            __syncwarp();
+            ++s_iter;
+            return true;
+        };
+        auto next_item = [&](int from) -> int {
+            int item = from;
+            while (item < num_items &&
+                   decode_item(item, qtiles, heads, length, lengths).tiles == 0)
+                item += gridDim.x;
+            return item;
+        };
+        // The first score MMAs of an item: wait for its biased queries, then S(0).
+        auto start_item = [&](int item) -> bool {
+            const Item it = decode_item(item, qtiles, heads, length, lengths);
+            if (!wait(kBarQReady, q_iter & 1)) return false;
+            ++q_iter;
+            return issue_s(true, it.tiles == 1);
+        };
+        int item = next_item(blockIdx.x);
+        if (item < num_items) ok = start_item(item);
+        while (ok && item < num_items) {
+            const Item it = decode_item(item, qtiles, heads, length, lengths);
+            // The candidate's length load is issued now and consumed at the last tile.
+            const int cand = item + gridDim.x;
+            const int cand_len = cand < num_items ? __ldg(lengths + cand / (qtiles * heads)) : 0;
+            int next = num_items;
+            for (int j = 0; j < it.tiles && ok; ++j) {
+                if (j + 1 == it.tiles && cand < num_items)
+                    next = cand_len > 0 ? cand : next_item(cand);
+                // Keep the tensor pipe fed: the next tile's (or next item's) score
+                // MMAs go ahead of this tile's P.V.
+                if (j + 1 < it.tiles) {
+                    if (!(ok = issue_s(false, j + 2 == it.tiles))) break;
+                } else if (next < num_items) {
+                    if (!(ok = start_item(next))) break;
+                }
+                if (!(ok = wait(kBarPFull, v_iter & 1))) break;
+                if (!(ok = wait(kBarVFull, v_iter & 1))) break;
+                if (j == 0 && items_done > 0 && !(ok = wait(kBarOFree, (items_done - 1) & 1)))
+                    break;
+                tc_fence_after();
+                if (elect_one()) {
 #pragma unroll
-                    for (int ks = 0; ks < kN / 16; ++ks) {
-                        const uint32_t a = ks >> 2, koff = (ks & 3) * 32;
-                        const uint64_t pd = sw128_desc(sbase + kSmemP + a * kAtom + koff, 16, 1024);
-                        // V is MN-major (head dim contiguous): 16 keys = 2 row groups = 2048 B;
-                        // the two 64-channel halves are kAtom apart.
-                        const uint64_t vd = sw128_desc(sbase + kSmemV + ks * 2048, kAtom, 1024);
-                        umma_f16_ss(tmem + kColO, pd, vd, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
-                    }
+                    for (uint32_t ks = 0; ks < kN / 16; ++ks)
+                        umma_f16_ss(tmem + kColO, d_p + kstep(ks),
+                                    d_v + static_cast<uint64_t>((ks * 2048) >> 4), idesc_o,
+                                    (j > 0 || ks > 0) ? 1u : 0u);
                     umma_commit(sync.bar(kBarVEmpty));
                     umma_commit(sync.bar(kBarODone));
-                    ++v_iter;
                 }
-                ++items_done;
+                __syncwarp();
+                ++v_iter;
             }
-            // Drain every MMA this thread issued before the CTA releases TMEM.
+            ++items_done;
+            item = next;
+        }
+        // Drain every MMA this warp issued before the CTA releases TMEM.
+        if (elect_one()) {
             umma_commit(sync.bar(kBarDrain));
             mbar_wait(sync.bar(kBarDrain), 0);
         }
+        __syncwarp();
     } else {
         // ---- softmax warps ---------------------------------------------------------------
         const int group = warp & 3;      // TMEM lane group == rows 32*group ..
@@ -374,55 +534,45 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
         const uint32_t tmem_row = tmem + (static_cast<uint32_t>(group * 32) << 16);
         const uint32_t shift = 31u - static_cast<uint32_t>(lane);
         const uint32_t pair_bar = 1 + group;  // named barrier of the two warps sharing rows
-        uint32_t q_iter = 0, s_iter = 0, o_iter = 0;
+        uint32_t q_iter = 0, s_iter = 0, o_iter = 0, h_base = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-            const Item it = decode_item(item, qtiles, heads, length, lengths);
-            const int row_q = it.q0 + row;
-            T* orow = out + (static_cast<int64_t>(it.n) * length + row_q) * C + it.h * kD +
-                      half * 64;
-            if (it.tiles == 0) {  // no valid key: the reference defines the rows as zero
+
+        // Items with no valid key are zero rows (reference :478-486); they need no MMA.
+        auto next_item = [&](int from) -> int {
+            int item = from;
+            for (; item < num_items; item += gridDim.x) {
+                const Item it = decode_item(item, qtiles, heads, length, lengths);
+                if (it.tiles > 0) break;
+                const int row_q = it.q0 + row;
                 if (row_q < length) {
+                    T* orow = out + (static_cast<int64_t>(it.n) * length + row_q) * C +
+                              it.h * kD + half * 64;
                     const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
                     for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(orow)[c] = z;
                 }
-                continue;
             }
-            // (Q+u), (Q+v) in fp32, rounded to T (reference .cu:268-281); this warp does
-            // head channels [64*half, 64*half+64) of its 32 rows.
-            if (!(ok = sync.wait_warp(kBarQFull, q_iter & 1))) break;
+            return item;
+        };
+        auto prepare_queries = [&](int item) -> bool {
+            const Item it = decode_item(item, qtiles, heads, length, lengths);
+            if (!sync.wait_warp(kBarQFull, q_iter & 1)) return false;
             ++q_iter;
-            {
-                const T* ub = ubias + it.h * kD;
-                const T* vb = vbias + it.h * kD;
-#pragma unroll 2
-                for (int c8 = 0; c8 < 8; ++c8) {
-                    const int c = half * 8 + c8;
-                    const uint32_t off = half * kAtom + sw128_offset(row, c8);
-                    const uint4 qw = *reinterpret_cast<const uint4*>(smem + kSmemQu + off);
-                    const uint4 uw4 = *reinterpret_cast<const uint4*>(ub + c * 8);
-                    const uint4 vw4 = *reinterpret_cast<const uint4*>(vb + c * 8);
-                    const uint32_t qs[4] = {qw.x, qw.y, qw.z, qw.w};
-                    const uint32_t us[4] = {uw4.x, uw4.y, uw4.z, uw4.w};
-                    const uint32_t vs[4] = {vw4.x, vw4.y, vw4.z, vw4.w};
-                    uint32_t a[4], b[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 q = unpack2<T>(qs[e]);
-                        const float2 u = unpack2<T>(us[e]);
-                        const float2 v = unpack2<T>(vs[e]);
-                        a[e] = pack2<T>(q.x + u.x, q.y + u.y);
-                        b[e] = pack2<T>(q.x + v.x, q.y + v.y);
-                    }
-                    *reinterpret_cast<uint4*>(smem + kSmemQu + off) = make_uint4(a[0], a[1], a[2], a[3]);
-                    *reinterpret_cast<uint4*>(smem + kSmemQv + off) = make_uint4(b[0], b[1], b[2], b[3]);
-                }
-            }
+            bias_queries<T>(smem, ubias + it.h * kD, vbias + it.h * kD, row, half);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(sync.bar(kBarQReady));
+            return true;
+        };
 
+        int item = next_item(blockIdx.x);
+        if (item < num_items) ok = prepare_queries(item);
+        while (ok && item < num_items) {
+            const Item it = decode_item(item, qtiles, heads, length, lengths);
+            // The candidate's length load is issued now and consumed at the last tile.
+            const int cand = item + gridDim.x;
+            const int cand_len = cand < num_items ? __ldg(lengths + cand / (qtiles * heads)) : 0;
+            int next = num_items;
             float m_run = -INFINITY;  // reference max (base-2 logits)
             float l_run = 0.0f;       // this half's running sum of 2^(logit - m_run)
             for (int j = 0; j < it.tiles; ++j) {
@@ -432,18 +582,23 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 tc_fence_after();
                 float s[kHalfKeys];
                 const int nvalid = it.valid - k0;  // valid keys in this tile (>= 1)
+                const uint32_t slot_lo = (h_base + j) & 1;
                 if (nvalid >= kN)
-                    load_logits<false>(s, tmem_row, group, half, shift, scale_log2, nvalid);
+                    load_logits<false>(s, tmem_row, group, half, shift, slot_lo, scale_log2, nvalid);
                 else
-                    load_logits<true>(s, tmem_row, group, half, shift, scale_log2, nvalid);
+                    load_logits<true>(s, tmem_row, group, half, shift, slot_lo, scale_log2, nvalid);
                 // Scores are in registers: the MMA warp may overwrite S with the next tile.
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(sync.bar(kBarSFree));
+                // After the last tile's scores, prepare the next item's queries so its
+                // first MMAs run under this item's exponentials and epilogue.
+                if (j + 1 == it.tiles && cand < num_items) {
+                    next = cand_len > 0 ? cand : next_item(cand);
+                    if (next < num_items && !(ok = prepare_queries(next))) break;
+                }
 
-                float m_half = -INFINITY;
-#pragma unroll
-                for (int e = 0; e < kHalfKeys; ++e) m_half = fmaxf(m_half, s[e]);
+                const float m_half = tree_max(s);
                 xchg[half * kM + row] = m_half;
                 named_barrier(pair_bar, 64);
                 const float m_tile = fmaxf(m_half, xchg[(1 - half) * kM + row]);
@@ -459,7 +614,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                     ++o_iter;
                     tc_fence_after();
                 }
-                float l_tile = 0.0f;
+                float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                 for (int c = 0; c < kHalfKeys / 8; ++c) {
                     uint32_t w[4];
@@ -467,14 +622,14 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                     for (int e = 0; e < 4; ++e) {
                         const float p0 = fast_exp2(s[c * 8 + 2 * e] - m_new);
                         const float p1 = fast_exp2(s[c * 8 + 2 * e + 1] - m_new);
-                        l_tile += p0 + p1;
+                        lsum[e] += p0 + p1;
                         w[e] = pack2<T>(p0, p1);
                     }
                     const uint32_t off = half * kAtom + sw128_offset(row, c);
                     *reinterpret_cast<uint4*>(smem + kSmemP + off) =
                         make_uint4(w[0], w[1], w[2], w[3]);
                 }
-                l_run = l_run * corr + l_tile;
+                l_run = l_run * corr + ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
                 m_run = m_new;
                 if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
@@ -497,6 +652,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 if (lane == 0) mbar_arrive(sync.bar(kBarPFull));
             }
             if (!ok) break;
+            h_base += it.tiles + 1;
             // ---- epilogue: combine the two halves' sums, wait for the last PV, O / l ------------
             xchg[half * kM + row] = l_run;
             named_barrier(pair_bar, 64);
@@ -506,7 +662,10 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
             ++o_iter;
             tc_fence_after();
             const float inv = 1.0f / l_total;
+            const int row_q = it.q0 + row;
             const bool store = row_q < length;
+            T* orow = out + (static_cast<int64_t>(it.n) * length + row_q) * C + it.h * kD +
+                      half * 64;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t o[32];
@@ -527,6 +686,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(sync.bar(kBarOFree));
+            item = next;
         }
     }
 
@@ -590,7 +750,7 @@ cudaError_t parakeet_tc_typed(const ParakeetProblem& p, cudaStream_t stream) {
     {
         const cuuint64_t dims[2] = {C, static_cast<cuuint64_t>(2 * p.length - 1)};
         const cuuint64_t strides[1] = {C * sizeof(T)};
-        const cuuint32_t box[2] = {64, kBand};
+        const cuuint32_t box[2] = {64, kN};
         const cuuint32_t estr[2] = {1, 1};
         if (encode(&pos_map, dt, 2, const_cast<void*>(p.position), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
