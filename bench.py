@@ -65,17 +65,23 @@ def load_peaks() -> dict:
                 source="fallback")
 
 
-def load_traffic(kernel_key: str):
-    """Per-launch DRAM bytes of ``kernel_key`` from the committed ncu summary, or None."""
+def load_traffic(kernel_key: str, algorithmic_bytes: float):
+    """DRAM bytes per launch of ``kernel_key``, scaled from the committed ncu capture.
+
+    ``profiles/dram_traffic.txt`` holds, per kernel, the ``dram__bytes_read.sum +
+    dram__bytes_write.sum`` of one captured launch and that launch's algorithmic bytes.
+    The capture is a smaller case than the benchmark's; traffic grows with the units
+    processed, so it is scaled by the ratio of algorithmic bytes. None if absent.
+    """
     path = REPO / "profiles" / "dram_traffic.txt"
     if not path.is_file():
         return None
     for line in path.read_text().splitlines():
         parts = line.split()
-        if len(parts) >= 2 and parts[0] == kernel_key and not line.startswith("#"):
+        if len(parts) >= 3 and parts[0] == kernel_key and not line.startswith("#"):
             try:
-                return float(parts[1])
-            except ValueError:
+                return float(parts[1]) / float(parts[2]) * algorithmic_bytes
+            except (ValueError, ZeroDivisionError):
                 return None
     return None
 
@@ -221,22 +227,45 @@ def build_zipformer(args, rank):
     return stacks, wl.zipformer_audio_seconds(input_lengths), total_bytes
 
 
+def zipformer_launch_bytes(stacks):
+    """(kernel, algorithmic bytes) of every launch of one step, in launch order."""
+    out = []
+    for heads, weights, layers, (out_self, out_nl) in stacks:
+        for L in layers:
+            n, t = L.projection.shape[:2]
+            nhtt = weights.numel() * 2
+            out.append(("zipformer_relative_attention",
+                        L.projection.numel() * 2 + L.position.numel() * 2 + L.mask.numel()
+                        + nhtt))
+            for v, o, h in ((L.value_a, out_self, heads), (L.value_b, out_self, heads),
+                            (L.nonlin_value, out_nl, 1)):
+                used = nhtt if h > 1 else n * t * t * 2
+                out.append(("zipformer_attention_value", used + v.numel() * 2 + o.numel() * 2))
+    return out
+
+
 def run_zipformer_step(stacks, stream, events=None):
     from fast_gpu_asr_b200.attention import zipformer_attention_value, zipformer_relative_attention
 
     j = 0
+
+    def mark(i):
+        if events is not None:
+            events[j][i].record(stream)
+
     for heads, weights, layers, (out_self, out_nl) in stacks:
         for L in layers:
-            if events is not None:
-                events[j][0].record(stream)
+            mark(0)
             zipformer_relative_attention(L.projection, L.position, L.mask, out=weights,
                                          stream=stream)
-            if events is not None:
-                events[j][1].record(stream)
-            zipformer_attention_value(weights, L.value_a, heads, out=out_self, stream=stream)
-            zipformer_attention_value(weights, L.value_b, heads, out=out_self, stream=stream)
-            zipformer_attention_value(weights, L.nonlin_value, 1, out=out_nl, stream=stream)
+            mark(1)
             j += 1
+            for v, o, h in ((L.value_a, out_self, heads), (L.value_b, out_self, heads),
+                            (L.nonlin_value, out_nl, 1)):
+                mark(0)
+                zipformer_attention_value(weights, v, h, out=o, stream=stream)
+                mark(1)
+                j += 1
 
 
 # ---- CPU legs (oracle port of the reference math) -----------------------------------------
@@ -360,16 +389,17 @@ def ours_arm(args, world, rank, local):
 
     if args.workload == "parakeet":
         layers, outs, audio, flops, nbytes = build_parakeet(args, rank)
-        n_launch = len(layers)
+        launch_kinds = [("parakeet_relative_attention", nbytes)] * len(layers)
 
         def step(events=None):
             run_parakeet_step(layers, outs, stream, events)
     else:
         stacks, audio, total_bytes = build_zipformer(args, rank)
-        n_launch = sum(len(s[2]) for s in stacks)
+        launch_kinds = zipformer_launch_bytes(stacks)
 
         def step(events=None):
             run_zipformer_step(stacks, stream, events)
+    n_launch = len(launch_kinds)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -377,7 +407,7 @@ def ours_arm(args, world, rank, local):
     stream.synchronize()
     variant = _lib.last_kernel_variant()
 
-    # Timed region: K steps, with per-launch events around the dominant kernel.
+    # Timed region: K steps, with events around every launch (on the launching stream).
     events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
                for _ in range(n_launch)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -387,55 +417,72 @@ def ours_arm(args, world, rank, local):
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    torch.cuda.nvtx.range_push("fga_timed")
     with torch.cuda.stream(stream):
         start.record(stream)
         for k in range(args.steps):
             step(events[k])
         end.record(stream)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     clocks = sampler.stop() if sampler else None
     barrier(world)
     elapsed_ms = start.elapsed_time(end)
     max_ms = allreduce_max(elapsed_ms, world)
-    launch_ms = [e[0].elapsed_time(e[1]) for ev in events for e in ev]
-    avg_launch_ms = float(np.mean(launch_ms))
+    launch_ms = np.array([[e[0].elapsed_time(e[1]) for e in ev] for ev in events])
 
     total_audio = audio * args.steps * world
     value = total_audio / (max_ms / 1000.0)
     ms_per_step = max_ms / args.steps
 
+    # Per-kernel totals over the timed steps; the roofline is reported for the kernel
+    # with the largest share of device time.
+    kernels = {}
+    for i, (name, nb) in enumerate(launch_kinds):
+        k = kernels.setdefault(name, {"ms": 0.0, "bytes": 0.0, "launches": 0})
+        k["ms"] += float(launch_ms[:, i].sum())
+        k["bytes"] += nb * args.steps
+        k["launches"] += args.steps
+    busy_ms = sum(k["ms"] for k in kernels.values())
+    shares = {name: k["ms"] / busy_ms for name, k in kernels.items()}
+    dominant = max(kernels, key=lambda n: kernels[n]["ms"])
+    dk = kernels[dominant]
+    avg_launch_ms = dk["ms"] / dk["launches"]
+    avg_bytes = dk["bytes"] / dk["launches"]
+
     if args.workload == "parakeet":
         achieved = flops / (avg_launch_ms / 1000.0) / 1e12
-        roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                    "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                    "traffic": load_traffic("parakeet_relative_attention"),
+        roofline = {"bound": "tensor", "kernel": dominant, "achieved": achieved,
+                    "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": achieved / peaks["bf16_tflops"],
+                    "traffic": load_traffic(dominant, avg_bytes),
                     "peak_source": f"{peaks['source']} bf16 dense (burst)",
                     "flops_per_launch": flops, "bytes_per_launch": nbytes,
                     "hbm_frac": nbytes / (avg_launch_ms / 1000.0) / 1e9 / peaks["hbm_gbs"],
                     "avg_launch_ms": avg_launch_ms, "variant": variant}
-        gpu_launches = args.steps * n_launch
     else:
-        # The dominant kernel is the weights kernel (writes the NHTT tensor).
-        wbytes = []
-        for heads, weights, layers, outs in stacks:
-            for L in layers:
-                n, t = L.projection.shape[:2]
-                wbytes.append(n * t * heads * 68 * 2 + (2 * t - 1) * heads * 8 + n * t
-                              + weights.numel() * 2)
-        per_launch = np.array(launch_ms).reshape(args.steps, n_launch).mean(axis=0)
-        achieved = float(np.sum(wbytes) / (np.sum(per_launch) / 1000.0) / 1e9)
-        roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
-                    "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                    "traffic": load_traffic("zipformer_relative_attention"),
+        achieved = dk["bytes"] / (dk["ms"] / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved,
+                    "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"],
+                    "traffic": load_traffic(dominant, avg_bytes),
                     "peak_source": f"{peaks['source']} HBM copy",
+                    "bytes_per_launch": avg_bytes, "avg_launch_ms": avg_launch_ms,
+                    "kernel_shares": shares,
+                    "kernel_hbm_frac": {n: k["bytes"] / (k["ms"] / 1000.0) / 1e9
+                                        / peaks["hbm_gbs"] for n, k in kernels.items()},
                     "step_bytes": total_bytes,
-                    "step_hbm_frac": total_bytes / (ms_per_step / 1000.0) / 1e9 / peaks["hbm_gbs"],
+                    "step_hbm_frac": total_bytes / (ms_per_step / 1000.0) / 1e9
+                    / peaks["hbm_gbs"],
                     "variant": variant}
-        gpu_launches = args.steps * n_launch * 4
+    gpu_launches = args.steps * n_launch
 
     e2e = None
-    if not args.no_e2e and args.workload == "parakeet":
-        e2e = e2e_parakeet(args, layers, audio, world)
+    if not args.no_e2e:
+        if args.workload == "parakeet":
+            e2e = e2e_parakeet(args, layers, audio, world)
+        else:
+            e2e = e2e_zipformer(args, stacks, audio, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -480,6 +527,67 @@ def e2e_parakeet(args, layers, audio, world):
                                         dev["position_bias"], dev["valid_lengths"],
                                         layers[0].scale, out=out, stream=stream)
             host_out.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    n = max(1, args.e2e_steps)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(n):
+            step()
+        end.record(stream)
+    torch.cuda.synchronize()
+    ms = allreduce_max(start.elapsed_time(end), world)
+    return {"value": audio * n * world / (ms / 1000.0), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n,
+            "ms_per_step": ms / n}
+
+
+def e2e_zipformer(args, stacks, audio, world):
+    """Same metric through the public API with pinned host inputs and outputs.
+
+    Per layer the step copies in the projection, positions, mask and the three value
+    inputs, runs the weights call and the three attention-value calls, and copies the
+    three attention outputs back. The NHTT weights stay on the device, as between two
+    plugins of an engine.
+    """
+    import torch
+
+    from fast_gpu_asr_b200.attention import zipformer_attention_value, zipformer_relative_attention
+
+    stream = torch.cuda.Stream()
+    names = ("projection", "position", "mask", "value_a", "value_b", "nonlin_value")
+    plan = []
+    h2d = d2h = 0
+    for heads, weights, layers, (out_self, out_nl) in stacks:
+        L0 = layers[0]
+        host = {k: getattr(L0, k).cpu().pin_memory() for k in names}
+        dev = {k: torch.empty_like(getattr(L0, k)) for k in names}
+        outs = [torch.empty_like(out_self), torch.empty_like(out_self), torch.empty_like(out_nl)]
+        host_outs = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+        plan.append((heads, weights, len(layers), host, dev, outs, host_outs))
+        h2d += sum(t.numel() * t.element_size() for t in host.values()) * len(layers)
+        d2h += sum(o.numel() * o.element_size() for o in outs) * len(layers)
+
+    def step():
+        for heads, weights, nlayers, host, dev, outs, host_outs in plan:
+            for _ in range(nlayers):
+                for k in names:
+                    dev[k].copy_(host[k], non_blocking=True)
+                zipformer_relative_attention(dev["projection"], dev["position"], dev["mask"],
+                                             out=weights, stream=stream)
+                zipformer_attention_value(weights, dev["value_a"], heads, out=outs[0],
+                                          stream=stream)
+                zipformer_attention_value(weights, dev["value_b"], heads, out=outs[1],
+                                          stream=stream)
+                zipformer_attention_value(weights, dev["nonlin_value"], 1, out=outs[2],
+                                          stream=stream)
+                for o, ho in zip(outs, host_outs):
+                    ho.copy_(o, non_blocking=True)
 
     with torch.cuda.stream(stream):
         step()
