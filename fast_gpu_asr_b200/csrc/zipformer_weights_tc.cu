@@ -1,27 +1,40 @@
-// Zipformer relative-position attention weights on tcgen05 tensor cores (f16/bf16).
+// Zipformer relative-position attention weights on tcgen05 tensor cores (f16/bf16, query
+// head dim 32, T <= 768).
 //
-// One CTA produces the weights of 128 query rows (q0 .. q0+127) of one (utterance n,
-// head h): W[n, h, q, k] for every key k < T. The content scores Q K^T (query head dim
-// 32, i.e. two K=16 steps) are computed by tcgen05.mma into TMEM, 128 keys at a time,
-// double-buffered (2 x 128 columns) so the next chunk's MMA runs while the threads
-// consume the current one. Thread i owns row q0+i (TMEM lane i) and adds the 4-dim
-// positional term sum_i pq[q,i] * pos[T-1-q+k, i] from an fp32 copy of the CTA's
-// positional band in shared memory (relative rows T-1-q0-127 .. T-1-q0+T-1).
+// W[n, h, q, k] = softmax_k( round_T(Q[q] . K[k]) + sum_i pq[q,i] * pos[T-1-q+k, i] ),
+// masked keys excluded, written as the I/O dtype T in the NHTT layout.
 //
-// Two passes over the key chunks (the QK^T MMAs are re-issued; at K = 32 they are far
-// cheaper than the output write):
-//   pass 1: logits -> online (max, sum) per row, masked keys excluded;
-//   pass 2: logits again -> exp(logit - max) / sum -> I/O dtype -> shared staging tile,
-//           then every warp writes whole row segments (coalesced, any alignment: the
-//           NHTT row stride T is not a multiple of 16 bytes for the encoder's lengths).
+// Launch shape: a persistent grid of one CTA per SM. A CTA takes (utterance, head) pairs
+// in a static stride and produces all query blocks (128 rows) of the pair, so Q and K of
+// the head are loaded once per pair by TMA (SWIZZLE_64B, rows past T read as zero).
+// 8 compute warps (two per TMEM lane quarter) + 1 control warp that issues TMA and MMAs.
 //
-// Reference semantics (zipformer_relative_attention_plugin.cu:238-327): the content
-// score is stored in the I/O dtype by the reference's GEMM, so it is rounded to T here
-// before the fp32 positional add; masked keys get weight 0; a row whose keys are all
-// masked is zero; rows q >= 7 with mask[q-7] (the padded-query halo) are zero; a row
-// whose sum is not positive (all logits -inf, or NaN) is zero.
+// TMEM (512 columns, one CTA per SM):
+//   [0, 128)    two 64-key score buffers (content scores Q K^T, fp32), filled by the
+//               control warp, drained by the compute warps (mbarrier ring);
+//   [128, 512)  the row's exponentials as packed f16 pairs, key k at column 128 + k/2.
+//
+// Per query block (thread = query row, warp sub-slot = which 32 keys of each chunk):
+//   pass 1: logits -> group max -> exp2(logit - running max) in fp32, summed in fp32 and
+//           cached in TMEM as f16 (no logit is computed twice); the running max of every
+//           32-key group is kept in shared memory;
+//   combine the two sub-slots' (max, sum) per row;
+//   pass 2: cached exps x exp(group max - row max) / sum -> T, staged per warp in shared
+//           memory and written as 16-byte stores aligned to the global NHTT addresses
+//           (the row stride T*2 bytes is not 16-byte aligned for the encoder's lengths, so
+//           each row's slots are re-aligned from the staging tile with byte permutes; the
+//           partial slots at range ends are written element-wise).
+//
+// Reference semantics (zipformer_relative_attention_plugin.cu:238-327 and 490-566): the
+// content score is stored in T by the reference GEMM (rounded here before the fp32
+// positional add, accumulated in the same order); max over valid keys; exp(x - max);
+// sum > 0 ? e / sum : 0; masked keys weigh 0; rows q >= 7 with mask[q-7] (the padded-
+// query halo) are zero; a row with no valid key is zero. The f16 exp cache perturbs a
+// weight by at most 2^-11 relative before the final rounding (at most one ulp of the
+// output type).
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "fga_common.cuh"
@@ -33,28 +46,59 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kM = 128;        // query rows per CTA
-constexpr int kChunk = 128;    // keys per MMA chunk
-constexpr int kQd = 32;        // query/key head dim served by this kernel
-constexpr int kMaxT = 768;     // keys held in shared memory (K tile rows)
-constexpr int kThreads = 128;
+constexpr int kQd = 32;             // query/key head dim served by this kernel
+constexpr int kMaxT = 768;          // keys held in shared memory / TMEM cache columns
+constexpr int kM = 128;             // query rows per block
+constexpr int kChunk = 64;          // keys per MMA (score buffer width)
+constexpr int kGroup = 32;          // keys per thread group
+constexpr int kMaxGroups = kMaxT / kGroup;
+constexpr int kSub = 2;             // compute warps per TMEM lane quarter
+constexpr int kComputeWarps = 4 * kSub;
+constexpr int kComputeThreads = 32 * kComputeWarps;
+constexpr int kThreads = kComputeThreads + 32;  // + control warp
 constexpr int kHalo = 7;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kCacheCol = 2 * kChunk;
+constexpr uint32_t kRowBytes = kQd * 2;  // 64-byte K-major rows (SWIZZLE_64B)
+
+// Positional band, kept in the I/O type (the positions are T values, so this is exact):
+// 4 planes (one per positional dim) x 4 copies shifted by 0..3 entries, so that every
+// thread reads 4 consecutive keys' values of a plane with one aligned 8-byte load. A
+// copy's stride is 16 (mod 64) elements, so the 16 lanes of a load phase (consecutive
+// rows, hence consecutive shifts) fall in distinct bank pairs.
+constexpr int kPlane = 904;
+constexpr int kCopy = 4 * kPlane + 48;
+constexpr int kBandFill = kMaxT + kM + 4;  // band entries written per block
+
+// Pass 2 works in 64-key pieces. Per-warp staging tile: 32 rows x (16-byte carry chunk +
+// 64 keys), 144-byte rows (an odd number of 16-byte chunks, so row-parallel 16-byte
+// stores are bank-conflict free).
+constexpr int kPiece = 64;
+constexpr int kStageRow = 16 + kPiece * 2;
+constexpr int kStageWarp = 32 * kStageRow;
+
+// Dynamic pair scheduling: each launch takes one of kSchedSlots (work, done) counter
+// pairs round-robin; the last CTA of a launch resets its pair to zero.
+constexpr int kSchedSlots = 64;
 
 // Shared memory (bytes from the 1024-aligned base).
-constexpr uint32_t kRowBytes = kQd * 2;                   // 64 B rows, 64-byte swizzle
-constexpr uint32_t kSmemQ = 0;                            // 128 rows
-constexpr uint32_t kSmemK = kSmemQ + kM * kRowBytes;      // up to kMaxT rows
-constexpr uint32_t kSmemStage = kSmemK + kMaxT * kRowBytes;  // [128 rows][128 keys] T
-constexpr uint32_t kStageRowBytes = kChunk * 2;
-constexpr uint32_t kSmemPos = kSmemStage + kM * kStageRowBytes;  // fp32x4 band rows
-constexpr uint32_t kMaxBandRows = kMaxT + kM;
-constexpr uint32_t kSmemMask = kSmemPos + kMaxBandRows * 16;     // valid-key bits
-constexpr uint32_t kSmemBar = kSmemMask + kMaxT / 8;
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemK = kSmemQ + kMaxT * kRowBytes;
+constexpr uint32_t kSmemBand = kSmemK + kMaxT * kRowBytes;
+constexpr uint32_t kSmemStage = kSmemBand + 4u * kCopy * 2u;
+constexpr uint32_t kSmemHist = kSmemStage + kComputeWarps * kStageWarp + 16;
+constexpr uint32_t kSmemStats = kSmemHist + kMaxGroups * kM * 4;
+constexpr uint32_t kSmemKb = kSmemStats + kSub * kM * 8;          // 2 buffers (pair parity)
+constexpr uint32_t kSmemValid = kSmemKb + 2 * kMaxT * 4;           // 2 buffers
+constexpr uint32_t kSmemLive = kSmemValid + 2 * kMaxGroups * 4;    // 2 buffers x 8 words
+constexpr uint32_t kSmemBar = kSmemLive + 2 * 8 * 4;
 constexpr uint32_t kSmemBytes = kSmemBar + 64;
-
-constexpr uint32_t kTmemCols = 256;
+static_assert(kCopy % 64 == 16, "band copy stride");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kMaxT / kM <= kComputeWarps, "one warp per query block computes its liveness");
 
 __device__ unsigned int g_zipformer_tc_error = 0;
+__device__ unsigned int g_zipformer_sched[2 * kSchedSlots];
 
 template <typename T> struct Fmt;
 template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
@@ -66,249 +110,501 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// a0 += q * lo(w), a1 += q * hi(w): T x T products accumulated in fp32 (exact products,
+// the same arithmetic as converting both operands to fp32 first).
+template <typename T> __device__ __forceinline__ void fma_pair(float& a0, float& a1, uint16_t q,
+                                                               uint32_t w);
+template <> __device__ __forceinline__ void fma_pair<__nv_bfloat16>(float& a0, float& a1,
+                                                                    uint16_t q, uint32_t w) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, %3, l, %0;\n\tfma.rn.f32.bf16 %1, %3, h, %1;\n\t}"
+        : "+f"(a0), "+f"(a1) : "r"(w), "h"(q));
+}
+template <> __device__ __forceinline__ void fma_pair<__half>(float& a0, float& a1, uint16_t q,
+                                                             uint32_t w) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "fma.rn.f32.f16 %0, %3, l, %0;\n\tfma.rn.f32.f16 %1, %3, h, %1;\n\t}"
+        : "+f"(a0), "+f"(a1) : "r"(w), "h"(q));
+}
+
+// Round two fp32 values to T and return them as fp32 (a GEMM that writes T).
+template <typename T> __device__ __forceinline__ float2 round_pair(float a, float b);
+template <> __device__ __forceinline__ float2 round_pair<__nv_bfloat16>(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(&v);
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+template <> __device__ __forceinline__ float2 round_pair<__half>(float a, float b) {
+    return __half22float2(__floats2half2_rn(a, b));
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack_pair(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack_pair<__half>(float a, float b) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_half2(uint32_t u) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+
 // SWIZZLE_64B K-major descriptor: 64-byte rows, 8-row groups of 512 bytes.
 __device__ __forceinline__ uint64_t sw64_desc(uint32_t smem_addr) {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>(1u) << 16;                   // LBO (unused for swizzled K-major)
+    d |= static_cast<uint64_t>(1u) << 16;                     // LBO (unused, swizzled K-major)
     d |= static_cast<uint64_t>((512u >> 4) & 0x3FFFu) << 32;  // SBO: 8 rows x 64 B
     d |= 1ull << 46;
-    d |= 4ull << 61;                                        // SWIZZLE_64B
+    d |= 4ull << 61;                                          // SWIZZLE_64B
     return d;
 }
 
+// Bounded wait with a warp-uniform result; a failure raises the CTA's abort word (the
+// CTA then skips all further work but keeps every barrier, so no thread is stranded).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
+                                          volatile uint32_t* abort) {
+    bool ok = (*abort == 0u) && mbar_wait(bar, parity);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && (threadIdx.x & 31) == 0) {
+        *abort = 1u;
+        atomicExch(&g_zipformer_tc_error, 1u);
+    }
+    return ok;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 1)
 zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             const T* __restrict__ proj, const T* __restrict__ pos,
-                            const uint8_t* __restrict__ mask, T* __restrict__ out, int length,
-                            int heads) {
+                            const uint8_t* __restrict__ mask, T* __restrict__ out, int seq,
+                            int heads, int num_pairs, int slot) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_load = sbase + kSmemBar;
-    const uint32_t bar_mma0 = sbase + kSmemBar + 8;  // + 8 * buffer
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 24);
-    float4* pos_band = reinterpret_cast<float4*>(smem + kSmemPos);
-    uint32_t* valid_bits = reinterpret_cast<uint32_t*>(smem + kSmemMask);
+    const uint32_t bar_kq = sbase + kSmemBar;
+    const uint32_t bar_full = sbase + kSmemBar + 8;   // + 8 * buffer
+    const uint32_t bar_free = sbase + kSmemBar + 24;  // + 8 * buffer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 40);
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + kSmemBar + 44);
+    uint16_t* band = reinterpret_cast<uint16_t*>(smem + kSmemBand);
+    volatile int* next_pair = reinterpret_cast<volatile int*>(smem + kSmemBar + 48);  // [2]
+    float* hist = reinterpret_cast<float*>(smem + kSmemHist);
+    float2* stats = reinterpret_cast<float2*>(smem + kSmemStats);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const int q0 = blockIdx.x * kM;
-    const int h = blockIdx.y;
-    const int n = blockIdx.z;
-    const int seq = length;
+    const bool control = warp == kComputeWarps;
+    const int qtr = warp & 3;
+    const int sub = warp >> 2;
+    const int q_local = qtr * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(qtr * 32) << 16;
     const int pdim = heads * (2 * kQd + 4);
+    const int ngroups = (seq + kGroup - 1) / kGroup;
     const int nchunks = (seq + kChunk - 1) / kChunk;
-    const int band_lo = seq - 1 - q0 - (kM - 1);  // relative row of band entry 0
-    const int band_rows = seq + kM - 1;
-    const int q = q0 + tid;
-    const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
+    const int nqb = (seq + kM - 1) / kM;
+    const int npieces = (seq + kPiece - 1) / kPiece;
+    const int split = (npieces + 1) / 2;  // pass-2 piece ranges: [0, split), [split, npieces)
 
     if ((sbase & 1023u) != 0) {
         if (tid == 0) atomicExch(&g_zipformer_tc_error, 2u);
         return;
     }
     if (tid == 0) {
-        mbar_init(bar_load, 1);
-        mbar_init(bar_mma0, 1);
-        mbar_init(bar_mma0 + 8, 1);
+        mbar_init(bar_kq, 1);
+        mbar_init(bar_full, 1);
+        mbar_init(bar_full + 8, 1);
+        mbar_init(bar_free, kComputeWarps);
+        mbar_init(bar_free + 8, kComputeWarps);
+        *abort = 0u;
         fence_mbar_init();
         prefetch_tensormap(&proj_map);
-        // Q rows q0.. (head h), then all K rows of head h. Rows past T read as zero.
-        mbar_expect_tx(bar_load, (kM + nchunks * kChunk) * kRowBytes);
-        tma_load_3d(sbase + kSmemQ, &proj_map, bar_load, h * kQd, q0, n);
-        for (int c = 0; c < nchunks; ++c)
-            tma_load_3d(sbase + kSmemK + c * kChunk * kRowBytes, &proj_map, bar_load,
-                        heads * kQd + h * kQd, c * kChunk, n);
     }
-    __syncwarp();
     if (warp == 0) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
         tmem_relinquish();
-    }
-    // Positional band (fp32) and valid-key bits, while the TMA runs.
-    for (int r = tid; r < band_rows; r += kThreads) {
-        const int rel = band_lo + r;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (rel >= 0 && rel < 2 * seq - 1) {
-            const T* pr = pos + (static_cast<int64_t>(rel) * heads + h) * 4;
-            v = make_float4(to_f32<T>(pr[0]), to_f32<T>(pr[1]), to_f32<T>(pr[2]),
-                            to_f32<T>(pr[3]));
-        }
-        pos_band[r] = v;
-    }
-    for (int w = tid; w < (nchunks * kChunk) / 32; w += kThreads) {
-        uint32_t bits = 0;
-        for (int b = 0; b < 32; ++b) {
-            const int k = w * 32 + b;
-            if (k < seq && !mrow[k]) bits |= 1u << b;
-        }
-        valid_bits[w] = bits;
-    }
-    // This row's positional query and halo state.
-    float pq0 = 0.f, pq1 = 0.f, pq2 = 0.f, pq3 = 0.f;
-    bool row_live = q < seq;
-    if (row_live) {
-        const T* pr = proj + (static_cast<int64_t>(n) * seq + q) * pdim + 2 * heads * kQd + h * 4;
-        pq0 = to_f32<T>(pr[0]);
-        pq1 = to_f32<T>(pr[1]);
-        pq2 = to_f32<T>(pr[2]);
-        pq3 = to_f32<T>(pr[3]);
-        if (q >= kHalo && mrow[q - kHalo]) row_live = false;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const bool loaded = mbar_wait(bar_load, 0);
-    bool ok = !__syncthreads_or(!loaded);
 
-    constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, kM, kChunk, 0, 0);
-    const uint64_t dq = sw64_desc(sbase + kSmemQ);
-    auto issue = [&](int it) {  // MMA for pass-iteration it into buffer it % 2
-        const int c = it % nchunks;
-        const uint64_t dk = sw64_desc(sbase + kSmemK + c * kChunk * kRowBytes);
-        const uint32_t d = tmem + (it & 1) * kChunk;
-        umma_f16_ss(d, dq, dk, idesc, 0);
-        umma_f16_ss(d, dq + 2, dk + 2, idesc, 1);  // second K=16 step: +32 bytes
-        umma_commit(bar_mma0 + 8 * (it & 1));
-    };
-    if (ok && warp == 0) {
-        tc_fence_after();
-        if (elect_one()) issue(0);
-        __syncwarp();
-    }
+    uint32_t ucount = 0;    // score-buffer uses so far (both roles count identically)
+    uint32_t kq_phase = 0;  // control warp: Q/K loads so far
+#pragma unroll 1
+    for (int iter = 0;; ++iter) {
+        if (tid == 0) next_pair[iter & 1] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
+        named_barrier(1, kThreads);
+        const int pair = next_pair[iter & 1];
+        if (pair >= num_pairs) break;
+        const int n = pair / heads;
+        const int h = pair - n * heads;
+        const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
+        const int buf = iter & 1;
+        float* kb = reinterpret_cast<float*>(smem + kSmemKb) + buf * kMaxT;
+        uint32_t* valid = reinterpret_cast<uint32_t*>(smem + kSmemValid) + buf * kMaxGroups;
+        uint32_t* live_q = reinterpret_cast<uint32_t*>(smem + kSmemLive) + buf * 8;
 
-    float m_run = -INFINITY, l_run = 0.0f, inv = 0.0f;
-    const int iters = 2 * nchunks;
-    const int prow = (kM - 1) - tid;  // band entry of key 0 for this row: seq-1-q - band_lo
+        if (!control) {
+            // Key validity (bit per key, +-inf bias per key) and query-block liveness.
 #pragma unroll 1
-    for (int it = 0; it < iters && ok; ++it) {
-        const int c = it % nchunks;
-        const bool pass2 = it >= nchunks;
-        const int k0 = c * kChunk;
-        // Buffer (it+1)%2 was last read at it-1: every thread has passed that point.
-        tc_fence_before();
-        __syncthreads();
-        if (it + 1 < iters && warp == 0) {
-            tc_fence_after();
-            if (elect_one()) issue(it + 1);
-            __syncwarp();
+            for (int g = warp; g < ngroups; g += kComputeWarps) {
+                const int k = g * kGroup + lane;
+                const bool v = k < seq && mrow[k] == 0;
+                const uint32_t bits = __ballot_sync(0xffffffffu, v);
+                kb[k] = v ? INFINITY : -INFINITY;
+                if (lane == 0) valid[g] = bits;
+            }
+            if (warp < nqb) {
+                bool any = false;
+                for (int q = warp * kM + lane; q < min(seq, warp * kM + kM); q += 32)
+                    any |= !(q >= kHalo && mrow[q - kHalo] != 0);
+                any = __any_sync(0xffffffffu, any);
+                if (lane == 0) live_q[warp] = any ? 1u : 0u;
+            }
+        } else if (ucount > 0) {
+            // Q/K of the previous pair are read by its MMAs: wait for the last one.
+            const uint32_t u = ucount - 1;
+            warp_wait(bar_full + 8 * (u & 1), (u >> 1) & 1, abort);
         }
-        // A row whose sum is not positive (no valid key, all -inf, or NaN) is zero, as in
-        // the reference (sum > 0 ? v / sum : 0).
-        if (pass2 && c == 0) inv = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
-        if (!mbar_wait(bar_mma0 + 8 * (it & 1), (it >> 1) & 1)) {
-            atomicExch(&g_zipformer_tc_error, 1u);
-            ok = false;
-        }
-        if (__syncthreads_or(!ok)) {
-            ok = false;
-            break;
-        }
-        tc_fence_after();
-        const uint32_t buf = tmem + lane_off + (it & 1) * kChunk;
-        uint8_t* srow = smem + kSmemStage + tid * kStageRowBytes;
-        float m_chunk = -INFINITY;
-        float s[32];
-#pragma unroll 1
-        for (int sub = 0; sub < kChunk / 32; ++sub) {
-            const uint32_t vbits = valid_bits[(k0 >> 5) + sub];
-            // Skip decisions are warp-uniform: tcgen05.ld is a warp-collective instruction.
-            const bool lane_any = row_live && vbits != 0u && (!pass2 || inv > 0.0f);
-            if (!__any_sync(0xffffffffu, lane_any)) {
-                if (pass2) {  // fully masked group or dead rows: zeros
-#pragma unroll
-                    for (int e = 0; e < 32; e += 8) {
-                        const uint32_t chunk = (sub * 4 + (e >> 3)) ^ (tid & 15);
-                        *reinterpret_cast<uint4*>(srow + chunk * 16) = make_uint4(0, 0, 0, 0);
+        named_barrier(1, kThreads);  // mask information of this pair is visible
+
+        bool any_valid = false;
+        for (int g = 0; g < ngroups; ++g) any_valid |= valid[g] != 0u;
+        uint32_t live_mask = 0;
+        for (int b = 0; b < nqb; ++b)
+            if (any_valid && live_q[b] != 0u) live_mask |= 1u << b;
+
+        if (control) {
+            // ---- control warp: Q/K loads and the score MMAs of every live block ----
+            if (live_mask != 0u && __all_sync(0xffffffffu, *abort == 0u)) {
+                if (lane == 0) {
+                    mbar_expect_tx(bar_kq, 2u * nqb * kM * kRowBytes);
+                    for (int b = 0; b < nqb; ++b) {
+                        tma_load_3d(sbase + kSmemQ + b * kM * kRowBytes, &proj_map, bar_kq,
+                                    h * kQd, b * kM, n);
+                        tma_load_3d(sbase + kSmemK + b * kM * kRowBytes, &proj_map, bar_kq,
+                                    heads * kQd + h * kQd, b * kM, n);
                     }
                 }
-                continue;
+                __syncwarp();
+                warp_wait(bar_kq, kq_phase & 1, abort);
+                ++kq_phase;
             }
-            uint32_t r[32];
-            tmem_ld32(buf + sub * 32, r);
-            tmem_wait_ld();
-            reg_fence(r);
-            const float4* pb = pos_band + prow + k0 + sub * 32;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const float4 p = pb[e];
-                float v = round_to<T>(__uint_as_float(r[e]));
-                v = fmaf(pq0, p.x, v);
-                v = fmaf(pq1, p.y, v);
-                v = fmaf(pq2, p.z, v);
-                v = fmaf(pq3, p.w, v);
-                const bool valid = lane_any && ((vbits >> e) & 1u);
-                s[e] = valid ? v : -INFINITY;
+            constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, kM, kChunk, 0, 0);
+#pragma unroll 1
+            for (int b = 0; b < nqb; ++b) {
+                if (!((live_mask >> b) & 1u)) continue;
+                const uint64_t dq = sw64_desc(sbase + kSmemQ + b * kM * kRowBytes);
+#pragma unroll 1
+                for (int j = 0; j < nchunks; ++j) {
+                    const uint32_t u = ucount + j;
+                    const uint32_t sb = u & 1;
+                    bool ok = __all_sync(0xffffffffu, *abort == 0u);
+                    if (ok && u >= 2) ok = warp_wait(bar_free + 8 * sb, ((u >> 1) - 1) & 1, abort);
+                    if (ok) {
+                        tc_fence_after();
+                        if (elect_one()) {
+                            const uint64_t dk = sw64_desc(sbase + kSmemK + j * kChunk * kRowBytes);
+                            const uint32_t d = tmem + sb * kChunk;
+                            umma_f16_ss(d, dq, dk, idesc, 0);
+                            umma_f16_ss(d, dq + 2, dk + 2, idesc, 1);  // second K=16 step
+                            umma_commit(bar_full + 8 * sb);
+                        }
+                        __syncwarp();
+                    }
+                }
+                ucount += nchunks;
             }
-            if (!pass2) {
-                float mm = -INFINITY;
+            continue;
+        }
+
+        // ---- compute warps ----
+#pragma unroll 1
+        for (int b = 0; b < nqb; ++b) {
+            const int q0 = b * kM;
+            const int q = q0 + q_local;
+            const bool block_live = (live_mask >> b) & 1u;
+            bool row_live = false;
+            float m_fin = -INFINITY, inv = 0.0f;
+            if (block_live) {
+                named_barrier(2, kComputeThreads);  // previous block's band/cache readers done
+                // Positional band of this block: entry i is relative row T-1-q0-127+i.
+                const int band_lo = seq - 1 - q0 - (kM - 1);
+#pragma unroll 1
+                for (int i = tid; i < kBandFill; i += kComputeThreads) {
+                    const int rel = band_lo + i;
+                    uint2 raw = make_uint2(0u, 0u);
+                    if (i < seq + kM - 1 && rel >= 0 && rel < 2 * seq - 1)
+                        raw = *reinterpret_cast<const uint2*>(pos + (static_cast<int64_t>(rel) * heads + h) * 4);
+                    const uint16_t v[4] = {static_cast<uint16_t>(raw.x & 0xFFFFu),
+                                           static_cast<uint16_t>(raw.x >> 16),
+                                           static_cast<uint16_t>(raw.y & 0xFFFFu),
+                                           static_cast<uint16_t>(raw.y >> 16)};
 #pragma unroll
-                for (int e = 0; e < 32; ++e) mm = fmaxf(mm, s[e]);
-                const float m_new = fmaxf(m_run, mm);
-                if (m_new != -INFINITY) {
-                    const float mb = m_new * kLog2e;
-                    float acc = 0.0f;
+                    for (int c = 0; c < 4; ++c) {
+                        if (i >= c) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) acc += fast_exp2(fmaf(s[e], kLog2e, -mb));
-                    l_run = l_run * fast_exp2(fmaf(m_run, kLog2e, -mb)) + acc;
+                            for (int pl = 0; pl < 4; ++pl)
+                                band[c * kCopy + pl * kPlane + i - c] = v[pl];
+                        }
+                    }
+                }
+                uint16_t pq[4] = {0, 0, 0, 0};
+                if (q < seq) {
+                    const uint2 raw = *reinterpret_cast<const uint2*>(
+                        proj + (static_cast<int64_t>(n) * seq + q) * pdim + 2 * heads * kQd + h * 4);
+                    pq[0] = static_cast<uint16_t>(raw.x & 0xFFFFu);
+                    pq[1] = static_cast<uint16_t>(raw.x >> 16);
+                    pq[2] = static_cast<uint16_t>(raw.y & 0xFFFFu);
+                    pq[3] = static_cast<uint16_t>(raw.y >> 16);
+                    row_live = !(q >= kHalo && mrow[q - kHalo] != 0);
+                }
+                const bool warp_live = __any_sync(0xffffffffu, row_live);
+                named_barrier(3, kComputeThreads);  // band complete
+                tc_fence_after();
+
+                // ---- pass 1 ----
+                const float2 l2e = make_float2(kLog2e, kLog2e);
+                const int prow = (kM - 1) - q_local;
+                float m_run = -INFINITY, l_run = 0.0f;
+#pragma unroll 1
+                for (int j = 0; j < nchunks; ++j) {
+                    const uint32_t u = ucount + j;
+                    const uint32_t sb = u & 1;
+                    const int g = 2 * j + sub;
+                    const uint32_t vb = g < ngroups ? valid[g] : 0u;
+                    const bool math = warp_live && vb != 0u;
+                    const bool ok = warp_wait(bar_full + 8 * sb, (u >> 1) & 1, abort);
+                    uint32_t r[32];
+                    if (ok && math) {
+                        tmem_ld32(tmem + lane_off + sb * kChunk + sub * kGroup, r);
+                        tmem_wait_ld();
+                        reg_fence(r);
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar_free + 8 * sb);
+                    if (!(ok && math)) {
+                        if (g < ngroups) hist[g * kM + q_local] = -INFINITY;
+                        continue;
+                    }
+                    float s[32];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 f = round_pair<T>(__uint_as_float(r[2 * i]),
+                                                       __uint_as_float(r[2 * i + 1]));
+                        s[2 * i] = f.x;
+                        s[2 * i + 1] = f.y;
+                    }
+                    // Positional term, accumulated in the reference's order (dims 0..3).
+                    const int b0 = prow + g * kGroup;
+                    const int cpy = b0 & 3;
+                    const uint16_t* bp = band + cpy * kCopy + (b0 - cpy);
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+#pragma unroll
+                        for (int pl = 0; pl < 4; ++pl) {
+                            const uint2 v = *reinterpret_cast<const uint2*>(bp + pl * kPlane + 4 * t);
+                            fma_pair<T>(s[4 * t], s[4 * t + 1], pq[pl], v.x);
+                            fma_pair<T>(s[4 * t + 2], s[4 * t + 3], pq[pl], v.y);
+                        }
+                    }
+                    if (vb != 0xffffffffu) {
+                        // Some keys of the group are masked or past T: min with -inf
+                        // removes them whatever their score (NaN included).
+                        const float* kp = kb + g * kGroup;
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            const float4 m4 = *reinterpret_cast<const float4*>(kp + 4 * t);
+                            s[4 * t] = fminf(s[4 * t], m4.x);
+                            s[4 * t + 1] = fminf(s[4 * t + 1], m4.y);
+                            s[4 * t + 2] = fminf(s[4 * t + 2], m4.z);
+                            s[4 * t + 3] = fminf(s[4 * t + 3], m4.w);
+                        }
+                    }
+                    float gm = max3(s[0], s[1], s[2]);
+#pragma unroll
+                    for (int e = 3; e < 31; e += 2) gm = max3(gm, s[e], s[e + 1]);
+                    gm = fmaxf(gm, s[31]);
+                    const float m_new = fmaxf(m_run, gm);
+                    const float mb = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
+                    const float2 nb = make_float2(-mb, -mb);
+                    float2 acc = make_float2(0.0f, 0.0f);
+                    uint32_t c16[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), l2e, nb);
+                        const float e0 = fast_exp2(x.x), e1 = fast_exp2(x.y);
+                        acc = __fadd2_rn(acc, make_float2(e0, e1));
+                        c16[i] = pack_half2(e0, e1);
+                    }
+                    const float alpha =
+                        m_run == m_new ? 1.0f : fast_exp2((m_run - m_new) * kLog2e);
+                    l_run = fmaf(l_run, alpha, acc.x + acc.y);
                     m_run = m_new;
+                    hist[g * kM + q_local] = m_new;
+                    tmem_st16(tmem + lane_off + kCacheCol + g * (kGroup / 2), c16);
                 }
-                (void)m_chunk;
-            } else {
-                const float mb = m_run * kLog2e;
+                ucount += nchunks;
+                tmem_wait_st();
+                stats[sub * kM + q_local] = make_float2(m_run, l_run);
+                tc_fence_before();
+                named_barrier(4, kComputeThreads);  // stats and the exp cache complete
+                tc_fence_after();
+                float l_fin = 0.0f;
 #pragma unroll
-                for (int e = 0; e < 32; e += 8) {
-                    uint32_t w[4];
+                for (int s2 = 0; s2 < kSub; ++s2) m_fin = fmaxf(m_fin, stats[s2 * kM + q_local].x);
 #pragma unroll
-                    for (int x = 0; x < 4; ++x) {
-                        const float a = s[e + 2 * x] == -INFINITY
-                                            ? 0.0f
-                                            : fast_exp2(fmaf(s[e + 2 * x], kLog2e, -mb)) * inv;
-                        const float b = s[e + 2 * x + 1] == -INFINITY
-                                            ? 0.0f
-                                            : fast_exp2(fmaf(s[e + 2 * x + 1], kLog2e, -mb)) * inv;
-                        const T ta = from_f32<T>(a), tb = from_f32<T>(b);
-                        w[x] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&ta)) |
-                               (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&tb)) << 16);
-                    }
-                    // 16-byte chunk (sub*4 + e/8) of this row, XOR-swizzled by row.
-                    const uint32_t chunk = (sub * 4 + (e >> 3)) ^ (tid & 15);
-                    *reinterpret_cast<uint4*>(srow + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+                for (int s2 = 0; s2 < kSub; ++s2) {
+                    const float2 st = stats[s2 * kM + q_local];
+                    l_fin += st.y * (st.x == m_fin ? 1.0f : fast_exp2((st.x - m_fin) * kLog2e));
                 }
+                // sum > 0 ? e / sum : 0 (no valid key, all -inf, NaN or +inf logits -> 0)
+                inv = l_fin > 0.0f ? 1.0f / l_fin : 0.0f;
+                row_live = row_live && inv > 0.0f;
             }
-        }
-        if (pass2) {
-            // Staging tile complete: write whole row segments, coalesced.
-            __syncthreads();
-            const int width = min(kChunk, seq - k0);
-            const int rows = min(kM, seq - q0);
-            T* obase = out + ((static_cast<int64_t>(n) * heads + h) * seq + q0) * seq + k0;
+
+            // ---- pass 2: this warp writes keys [kb_w, ke_w) of its 32 rows ----
+            const bool all_live = __all_sync(0xffffffffu, row_live);
+            const bool use_tmem = block_live && __any_sync(0xffffffffu, row_live) &&
+                                  __all_sync(0xffffffffu, *abort == 0u);
+            const int p_lo = sub == 0 ? 0 : split;
+            const int p_hi = sub == 0 ? split : npieces;
+            const int kb_w = p_lo * kPiece;
+            const int ke_w = min(p_hi * kPiece, seq);
+            const int rows_here = min(32, seq - (q0 + qtr * 32));
+            const int64_t e_base =
+                (static_cast<int64_t>(n * heads + h) * seq + q0 + qtr * 32) * seq;
+            uint8_t* stage_w = smem + kSmemStage + warp * kStageWarp;
+            uint8_t* srow = stage_w + lane * kStageRow;
+            auto group_valid = [&](int g) { return g < ngroups && valid[g] != 0u; };
+            auto piece_cached = [&](int pc) {
+                return use_tmem && (group_valid(2 * pc) || group_valid(2 * pc + 1));
+            };
+            uint32_t c[32];
+            if (p_lo < p_hi && piece_cached(p_lo))
+                tmem_ld32(tmem + lane_off + kCacheCol + p_lo * (kPiece / 2), c);
+            uint4 carry = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll 1
-            for (int rr = warp; rr < rows; rr += kThreads / 32) {
-                const uint8_t* src = smem + kSmemStage + rr * kStageRowBytes;
-                T* dst = obase + static_cast<int64_t>(rr) * seq;
-                for (int k = lane; k < width; k += 32) {
-                    const uint32_t chunk = (k >> 3) ^ (rr & 15);
-                    dst[k] = *reinterpret_cast<const T*>(src + chunk * 16 + (k & 7) * 2);
+            for (int pc = p_lo; pc < p_hi; ++pc) {
+                const int k0 = pc * kPiece;
+                uint32_t w[32];
+                if (piece_cached(pc)) {
+                    tmem_wait_ld();
+                    reg_fence(c);
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int g = 2 * pc + half;
+                        if (group_valid(g)) {
+                            const float hm = hist[g * kM + q_local];
+                            const float scale =
+                                row_live ? fast_exp2((hm - m_fin) * kLog2e) * inv : 0.0f;
+                            const float2 sc = make_float2(scale, scale);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float2 f = __fmul2_rn(unpack_half2(c[16 * half + i]), sc);
+                                w[16 * half + i] = pack_pair<T>(f.x, f.y);
+                            }
+                            if (!all_live) {
+#pragma unroll
+                                for (int i = 0; i < 16; ++i)
+                                    w[16 * half + i] = row_live ? w[16 * half + i] : 0u;
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) w[16 * half + i] = 0u;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) w[i] = 0u;
                 }
+                // Next piece's exps are read from TMEM while this one is written out.
+                if (pc + 1 < p_hi && piece_cached(pc + 1))
+                    tmem_ld32(tmem + lane_off + kCacheCol + (pc + 1) * (kPiece / 2), c);
+                *reinterpret_cast<uint4*>(srow) = carry;
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    *reinterpret_cast<uint4*>(srow + 16 + 16 * i) =
+                        make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                carry = make_uint4(w[28], w[29], w[30], w[31]);
+                __syncwarp();
+                // Staging element i of a row holds key k0 - 8 + i. A slot is an 8-element
+                // run whose start is 16-byte aligned in the output; slot m of this piece
+                // starts at key k0 - d + 8m, d = (row's element offset) mod 8.
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    const int row = it * 4 + (lane >> 3);
+                    const int m = lane & 7;
+                    if (row < rows_here) {
+                        const int64_t e_row = e_base + static_cast<int64_t>(row) * seq;
+                        const int d = static_cast<int>(e_row & 7);
+                        const int lo = k0 - d + 8 * m;
+                        const uint8_t* sr = stage_w + row * kStageRow;
+                        if (lo >= kb_w && lo + 8 <= ke_w) {
+                            const int s0 = 8 - d + 8 * m;
+                            const uint32_t* wp = reinterpret_cast<const uint32_t*>(sr) + (s0 >> 1);
+                            const uint32_t a0 = wp[0], a1 = wp[1], a2 = wp[2], a3 = wp[3], a4 = wp[4];
+                            const uint32_t sel = (s0 & 1) ? 0x5432u : 0x3210u;
+                            const uint4 o = make_uint4(__byte_perm(a0, a1, sel), __byte_perm(a1, a2, sel),
+                                                       __byte_perm(a2, a3, sel), __byte_perm(a3, a4, sel));
+                            *reinterpret_cast<uint4*>(out + e_row + lo) = o;
+                        } else if (lo + 8 > kb_w && lo < ke_w) {
+                            const T* se = reinterpret_cast<const T*>(sr);
+                            for (int k = max(lo, kb_w); k < min(lo + 8, ke_w); ++k)
+                                out[e_row + k] = se[k - k0 + 8];
+                        }
+                    }
+                }
+                if (pc + 1 == p_hi && lane < rows_here) {
+                    // Keys after the last slot of the range (slot m = 8, always partial).
+                    const int64_t e_row = e_base + static_cast<int64_t>(lane) * seq;
+                    const int d = static_cast<int>(e_row & 7);
+                    const int lo = k0 - d + kPiece;
+                    const T* se = reinterpret_cast<const T*>(srow);
+                    for (int k = max(lo, kb_w); k < min(lo + 8, ke_w); ++k)
+                        out[e_row + k] = se[k - k0 + 8];
+                }
+                __syncwarp();
             }
+            tc_fence_before();
         }
     }
-    // Drain: the last issued MMA is waited on in the loop; on an abort wait (bounded)
-    // for any outstanding one before releasing TMEM.
-    if (!ok && warp == 0 && elect_one()) {
-        mbar_wait(bar_mma0, 0);
-        mbar_wait(bar_mma0 + 8, 0);
+
+    // Teardown: the control warp waits (bounded) for its last MMA before TMEM is freed.
+    if (control && ucount > 0) {
+        const uint32_t u = ucount - 1;
+        if (!mbar_wait(bar_full + 8 * (u & 1), (u >> 1) & 1) && lane == 0)
+            atomicExch(&g_zipformer_tc_error, 1u);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+    if (tid == 0) {
+        // Every CTA has drawn past the last pair; the last one out resets the slot.
+        __threadfence();
+        if (atomicAdd(&g_zipformer_sched[2 * slot + 1], 1u) == gridDim.x - 1) {
+            atomicExch(&g_zipformer_sched[2 * slot], 0u);
+            atomicExch(&g_zipformer_sched[2 * slot + 1], 0u);
+        }
     }
 }
 
@@ -331,6 +627,14 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 0;
+    return n;
+}
+
 template <typename T>
 cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stream) {
     EncodeTiledFn encode = encode_fn();
@@ -342,7 +646,7 @@ cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stre
     const cuuint64_t dims[3] = {pdim, static_cast<cuuint64_t>(p.length),
                                 static_cast<cuuint64_t>(p.batch)};
     const cuuint64_t strides[2] = {pdim * sizeof(T), pdim * sizeof(T) * p.length};
-    const cuuint32_t box[3] = {kQd, kChunk, 1};
+    const cuuint32_t box[3] = {kQd, kM, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     if (encode(&map, dt, 3, const_cast<void*>(p.projection), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
@@ -357,10 +661,15 @@ cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stre
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    const dim3 grid((p.length + kM - 1) / kM, p.heads, p.batch);
+    const int64_t pairs = static_cast<int64_t>(p.batch) * p.heads;
+    const int sms = sm_count();
+    if (sms <= 0) return cudaErrorNotSupported;
+    const int grid = static_cast<int>(pairs < sms ? pairs : sms);
+    static std::atomic<unsigned int> ticket{0};
+    const int slot = static_cast<int>(ticket.fetch_add(1u) % kSchedSlots);
     zipformer_weights_tc_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(
         map, static_cast<const T*>(p.projection), static_cast<const T*>(p.position), p.mask,
-        static_cast<T*>(p.weights), p.length, p.heads);
+        static_cast<T*>(p.weights), p.length, p.heads, static_cast<int>(pairs), slot);
     return cudaGetLastError();
 }
 
@@ -369,10 +678,14 @@ cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stre
 cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem& p, cudaStream_t stream) {
     if (p.query_dim != kQd || (p.dtype != FGA_HALF && p.dtype != FGA_BF16))
         return cudaErrorNotSupported;
-    if (p.length > kMaxT || p.batch > 65535 || p.heads > 65535) return cudaErrorNotSupported;
-    // TMA needs 16-byte row strides: H * (2*32+4) * 2 bytes = 136 H.
+    if (p.length > kMaxT || p.length < 1) return cudaErrorNotSupported;
+    if (static_cast<int64_t>(p.batch) * p.heads > (1ll << 30)) return cudaErrorNotSupported;
+    // TMA needs 16-byte row strides (H * (2*32+4) * 2 bytes = 136 H) and a 16-byte aligned
+    // base; the aligned row writes need a 16-byte aligned output.
     const int64_t row_bytes = static_cast<int64_t>(p.heads) * (2 * kQd + 4) * 2;
-    if (row_bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(p.projection) & 15u) != 0)
+    if (row_bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(p.projection) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(p.weights) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(p.position) & 7u) != 0)
         return cudaErrorNotSupported;
     return p.dtype == FGA_HALF ? weights_tc_typed<__half>(p, stream)
                                : weights_tc_typed<__nv_bfloat16>(p, stream);
