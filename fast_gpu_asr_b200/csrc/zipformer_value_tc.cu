@@ -1,19 +1,24 @@
 // Zipformer attention-value on tcgen05 tensor cores (f16/bf16):
 //   out[n, q, h*hd + d] = sum_k A[n, ha, q, k] * V[n, k, h*hd + d],   ha = (heads == 1 ? 0 : h)
 //
-// One CTA computes 128 query rows of one (utterance n, value head h). The attention
-// rows are the dominant HBM stream. They cannot be fetched by TMA: the NHTT row stride T
-// is not a multiple of 16 bytes for the encoder's lengths. So every thread streams its own
-// row with aligned 16-byte loads, shifts it into place (rows start at any 2-byte
-// boundary) and writes it into a K-major SWIZZLE_128B tile (64 keys per chunk). V arrives
-// by TMA as an MN-major SWIZZLE_128B tile holding *all* C channels of the chunk's keys,
-// zero-padded to a multiple of 64; the MMA computes all C_pad output columns into TMEM
-// and the epilogue keeps the head's hd columns. At 4-12 MACs per attention element the
-// MMA is far from the limit; the extra columns cost nothing measurable.
+// One CTA computes 128 query rows of one (utterance n, value head h) (two CTAs per SM).
+// The attention rows are the dominant HBM stream. Their NHTT row stride (T*2 bytes) is
+// not 16-byte aligned for the encoder's lengths, so they are read by the threads: eight
+// lanes share one row's 64-key chunk, each loading two consecutive aligned 16-byte
+// pieces (so one warp instruction reads four 128-byte row segments), shifting its 8 keys
+// into place (rows start at any 2-byte boundary) and storing them into a K-major
+// SWIZZLE_128B tile. The next chunk's loads are issued before the current chunk is
+// shifted, so two chunks of loads are in flight per thread.
 //
-// Both A and V tiles are double-buffered: chunk c+1 is loaded while the MMA of chunk c
-// runs. Reference: zipformer_attention_value_plugin.cu:118-181 (fp32 accumulation; one
-// value head consumes attention head 0, :85).
+// Warps 0-7 load and repack (16 rows each); warp 8 issues the MMAs and the V loads. V
+// arrives by TMA as MN-major SWIZZLE_128B tiles of 64 channels starting at the head's
+// first channel rounded down to 8 (one tile for a 12-channel self-attention head,
+// ceil(C/64) for the NonlinAttention value); A tiles and V tiles are double-buffered.
+// The epilogue reads the fp32 accumulator from TMEM and stores the head's channels.
+//
+// All waits are bounded; a timeout raises the CTA's abort word, after which every warp
+// skips its work but keeps its loop. Reference: zipformer_attention_value_plugin.cu:
+// 118-181 (fp32 accumulation; one value head consumes attention head 0, :85).
 #include <cuda.h>
 
 #include <cstdint>
@@ -27,13 +32,13 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kM = 128;       // query rows per CTA
-constexpr int kKc = 64;       // keys per chunk (one 128-byte swizzle atom of A)
-constexpr int kThreads = 128;
+constexpr int kM = 128;        // query rows per CTA
+constexpr int kKc = 64;        // keys per chunk (one 128-byte swizzle atom of A)
+constexpr int kLoadWarps = 8;
+constexpr int kThreads = (kLoadWarps + 1) * 32;
 constexpr int kMaxCpad = 512;  // TMEM columns
-
-constexpr uint32_t kATile = kM * 128;        // 16 KB: 128 rows x 64 keys
-constexpr uint32_t kVAtom = kKc * 128;       // 8 KB: 64 keys x 64 channels
+constexpr uint32_t kATile = kM * 128;   // 16 KB: 128 rows x 64 keys
+constexpr uint32_t kVAtom = kKc * 128;  // 8 KB: 64 keys x 64 channels
 
 __device__ unsigned int g_value_tc_error = 0;
 
@@ -41,102 +46,139 @@ template <typename T> struct Fmt;
 template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
 template <> struct Fmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
 
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 struct Layout {
-    uint32_t a0, v0, bar, bytes, vtile;
+    uint32_t a0, v0, vstage, bar, bytes, tmem_cols;
 };
+
+__host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
+    return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
+}
 
 __host__ __device__ constexpr Layout make_layout(int cpad) {
     Layout l{};
-    l.vtile = static_cast<uint32_t>(cpad / 64) * kVAtom;
+    l.vstage = static_cast<uint32_t>(cpad / 64) * kVAtom;
     l.a0 = 0;
     l.v0 = 2 * kATile;
-    l.bar = l.v0 + 2 * l.vtile;
+    l.bar = l.v0 + 2 * l.vstage;
     l.bytes = l.bar + 64;
+    l.tmem_cols = pow2_cols(cpad);
     return l;
 }
 
-// Copy this thread's 64 attention values [e, e+64) (element offset e into the flat
-// attention tensor, any 2-byte alignment) into row `row` of the K-major swizzled tile.
-// Elements at or beyond `limit` (end of the row's valid keys) are zero.
-template <typename T>
-__device__ __forceinline__ void stage_row(uint8_t* tile, int row, const T* __restrict__ base,
-                                         int64_t e, int nkeys) {
-    const int a = static_cast<int>(e & 7);  // misalignment in elements
-    const uint4* src = reinterpret_cast<const uint4*>(base + (e - a));
-    uint32_t w[36];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) {
-        // The 9th vector is only needed when the row is misaligned.
-        const uint4 v = (i < 8 || a != 0) ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
-        w[4 * i] = v.x;
-        w[4 * i + 1] = v.y;
-        w[4 * i + 2] = v.z;
-        w[4 * i + 3] = v.w;
+// Bounded wait with a warp-uniform result; a failure raises the CTA's abort word.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
+                                          volatile uint32_t* abort) {
+    bool ok = (*abort == 0u) && mbar_wait(bar, parity);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && (threadIdx.x & 31) == 0) {
+        *abort = 1u;
+        atomicExch(&g_value_tc_error, 1u);
     }
-    // Shift by a elements: whole words (a >> 1) with a predicated barrel, then half a
-    // word with a funnel shift.
-    const uint32_t sw = static_cast<uint32_t>(a) >> 1;
+    return ok;
+}
+
+// This lane's share of one row chunk: the aligned 16-byte pieces at s and s+8 elements
+// (s = aligned span start + 8m). Elements past the end of the tensor read as zero.
+template <typename T>
+__device__ __forceinline__ void load_piece(const T* __restrict__ att, int64_t s,
+                                           int64_t att_elems, uint4 (&p)[2]) {
+    if (s + 16 <= att_elems) {
+        p[0] = __ldg(reinterpret_cast<const uint4*>(att + s));
+        p[1] = __ldg(reinterpret_cast<const uint4*>(att + s + 8));
+    } else {
+        uint32_t w[8];
+        const uint16_t* g = reinterpret_cast<const uint16_t*>(att);
 #pragma unroll
-    for (int i = 0; i < 34; ++i) w[i] = (sw & 2u) ? w[i + 2] : w[i];
+        for (int x = 0; x < 8; ++x) {
+            const uint32_t lo = s + 2 * x < att_elems ? g[s + 2 * x] : 0u;
+            const uint32_t hi = s + 2 * x + 1 < att_elems ? g[s + 2 * x + 1] : 0u;
+            w[x] = lo | (hi << 16);
+        }
+        p[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        p[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
+// Keys 8m..8m+7 of the chunk from the two pieces, shifted by a elements; keys at or past
+// nk (the end of the row) are zero.
+__device__ __forceinline__ uint4 shift_piece(const uint4 (&p)[2], int a, int m, int nk) {
+    const uint32_t w[8] = {p[0].x, p[0].y, p[0].z, p[0].w, p[1].x, p[1].y, p[1].z, p[1].w};
+    const uint32_t o = static_cast<uint32_t>(a) >> 1;
+    uint32_t x[7], y[5];
 #pragma unroll
-    for (int i = 0; i < 33; ++i) w[i] = (sw & 1u) ? w[i + 1] : w[i];
+    for (int k = 0; k < 7; ++k) x[k] = (o & 1u) ? w[k + 1] : w[k];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) y[k] = (o & 2u) ? x[k + 2] : x[k];
     const uint32_t sh = (a & 1) ? 16u : 0u;
+    uint32_t out[4];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) w[i] = __funnelshift_r(w[i], w[i + 1], sh);
-    // Zero keys beyond the row's end (last chunk).
-    if (nkeys < kKc) {
+    for (int i = 0; i < 4; ++i) out[i] = __funnelshift_r(y[i], y[i + 1], sh);
+    if (8 * m + 8 > nk) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int k = 2 * i;
-            if (k >= nkeys) w[i] = 0u;
-            else if (k + 1 >= nkeys) w[i] &= 0xFFFFu;
+        for (int i = 0; i < 4; ++i) {
+            const int k = 8 * m + 2 * i;
+            if (k >= nk) out[i] = 0u;
+            else if (k + 1 >= nk) out[i] &= 0xFFFFu;
         }
     }
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(tile + sw128_offset(row, c)) =
-            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
 zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map, const T* __restrict__ att,
-                          T* __restrict__ out, int length, int att_heads, int value_heads,
+                          T* __restrict__ out, int seq, int att_heads, int value_heads,
                           int channels, int cpad, int64_t att_elems) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
     const Layout L = make_layout(cpad);
-    const uint32_t bar_v0 = sbase + L.bar;        // + 8 * buffer: V tile loaded
-    const uint32_t bar_mma0 = sbase + L.bar + 16;  // + 8 * buffer: MMA of that buffer done
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + 32);
+    const uint32_t bar_afull = sbase + L.bar;        // + 8 * buffer (count kLoadWarps)
+    const uint32_t bar_aempty = sbase + L.bar + 16;  // + 8 * buffer (MMA commit)
+    const uint32_t bar_vfull = sbase + L.bar + 32;   // + 8 * buffer (TMA)
+    const uint32_t bar_acc = sbase + L.bar + 48;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + 56);
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + L.bar + 60);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
-    const int q0 = blockIdx.x * kM;
-    const int h = blockIdx.y;
-    const int n = blockIdx.z;
-    const int seq = length;
+    const int lane = tid & 31;
+    const int nqb = (seq + kM - 1) / kM;
+    const int q0 = (blockIdx.x % nqb) * kM;
+    const int h = (blockIdx.x / nqb) % value_heads;
+    const int n = blockIdx.x / (nqb * value_heads);
     const int hd = channels / value_heads;
     const int ha = value_heads == 1 ? 0 : h;
-    const int q = q0 + tid;
     const int nchunks = (seq + kKc - 1) / kKc;
-    const uint32_t tcols = cpad <= 64 ? 64 : cpad <= 128 ? 128 : cpad <= 256 ? 256 : 512;
+    const int col0 = h * hd;
+    const int col_base = col0 & ~7;
 
     if ((sbase & 1023u) != 0) {
         if (tid == 0) atomicExch(&g_value_tc_error, 2u);
         return;
     }
     if (tid == 0) {
-        mbar_init(bar_v0, 1);
-        mbar_init(bar_v0 + 8, 1);
-        mbar_init(bar_mma0, 1);
-        mbar_init(bar_mma0 + 8, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar_afull + 8 * b, kLoadWarps);
+            mbar_init(bar_aempty + 8 * b, 1);
+            mbar_init(bar_vfull + 8 * b, 1);
+        }
+        mbar_init(bar_acc, 1);
+        *abort = 0u;
         fence_mbar_init();
         prefetch_tensormap(&v_map);
     }
-    __syncwarp();
     if (warp == 0) {
-        tmem_alloc(smem_u32(tmem_slot), tcols);
+        tmem_alloc(smem_u32(tmem_slot), L.tmem_cols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -144,67 +186,28 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map, const T* __
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    auto load_v = [&](int c) {  // V chunk c -> buffer c & 1 (all channels, zero-padded)
-        const uint32_t b = c & 1;
-        mbar_expect_tx(bar_v0 + 8 * b, L.vtile);
-        for (int x = 0; x < cpad / 64; ++x)
-            tma_load_3d(sbase + L.v0 + b * L.vtile + x * kVAtom, &v_map, bar_v0 + 8 * b, x * 64,
-                        c * kKc, n);
-    };
-    if (tid == 0) {
-        load_v(0);
-        if (nchunks > 1) load_v(1);
-    }
-    // Row q of this CTA: element offset of A[n, ha, q, 0].
-    const int64_t row_e = ((static_cast<int64_t>(n) * att_heads + ha) * seq + q) * seq;
-    const bool row_live = q < seq;
-    const T* arow_base = att;
-    const uint32_t idesc_base = idesc_f16(Fmt<T>::v, kM, 16, 0, 1);  // N patched per part
-    bool ok = true;
-
-#pragma unroll 1
-    for (int c = 0; c < nchunks && ok; ++c) {
-        const uint32_t b = c & 1;
-        // A buffer b was last read by the MMA of chunk c-2.
-        if (c >= 2 && !mbar_wait(bar_mma0 + 8 * b, ((c - 2) >> 1) & 1)) ok = false;
-        if (__syncthreads_or(!ok)) { ok = false; break; }
-        uint8_t* tile = smem + L.a0 + b * kATile;
-        const int k0 = c * kKc;
-        const int nk = min(kKc, seq - k0);
-        if (row_live) {
-            // Stay inside the tensor: the last row's tail must not read past its end.
-            const int64_t e = row_e + k0;
-            const int a = static_cast<int>(e & 7);
-            if (e - a + 72 <= att_elems) {
-                stage_row<T>(tile, tid, arow_base, e, nk);
-            } else {
-                for (int cc = 0; cc < 8; ++cc) {
-                    uint32_t w[4];
-                    for (int x = 0; x < 4; ++x) {
-                        const int k = cc * 8 + 2 * x;
-                        const T lo = k < nk ? att[e + k] : from_f32<T>(0.f);
-                        const T hi = k + 1 < nk ? att[e + k + 1] : from_f32<T>(0.f);
-                        w[x] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
-                               (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
-                    }
-                    *reinterpret_cast<uint4*>(tile + sw128_offset(tid, cc)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
-                }
-            }
-        } else {
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc)
-                *reinterpret_cast<uint4*>(tile + sw128_offset(tid, cc)) = make_uint4(0, 0, 0, 0);
+    if (warp == kLoadWarps) {
+        // ---------------- MMA issuer and V producer ----------------
+        auto load_v = [&](int c) {
+            const uint32_t b = c & 1;
+            mbar_expect_tx(bar_vfull + 8 * b, L.vstage);
+            for (int x = 0; x < cpad / 64; ++x)
+                tma_load_3d(sbase + L.v0 + b * L.vstage + x * kVAtom, &v_map, bar_vfull + 8 * b,
+                            col_base + x * 64, c * kKc, n);
+        };
+        if (lane == 0) {
+            load_v(0);
+            if (nchunks > 1) load_v(1);
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (warp == 0) {
-            bool vok = mbar_wait(bar_v0 + 8 * b, (c >> 1) & 1);
-            vok = __all_sync(0xffffffffu, vok);
-            if (!vok) {
-                ok = false;
-            } else {
+        __syncwarp();
+        const uint32_t idesc_base = idesc_f16(Fmt<T>::v, kM, 16, 0, 1);  // N patched per part
+        int last_issued = -1;
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c) {
+            const uint32_t b = c & 1;
+            bool ok = warp_wait(bar_afull + 8 * b, (c >> 1) & 1, abort);
+            ok = ok && warp_wait(bar_vfull + 8 * b, (c >> 1) & 1, abort);
+            if (ok) {
                 tc_fence_after();
                 if (elect_one()) {
                     const uint64_t da = sw128_desc(sbase + L.a0 + b * kATile, 16, 1024);
@@ -212,54 +215,129 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map, const T* __
                         const int nw = min(256, cpad - part * 256);
                         const uint32_t idesc = idesc_base + ((static_cast<uint32_t>(nw) >> 3) << 17) -
                                                ((16u >> 3) << 17);
-                        // V: MN-major, 64-channel atoms kKc*128 bytes apart, 16 keys = 2048 B.
-                        const uint64_t dv = sw128_desc(
-                            sbase + L.v0 + b * L.vtile + part * 4 * kVAtom, kVAtom, 1024);
+                        // V: MN-major, 64-channel atoms kVAtom bytes apart, 16 keys = 2048 B.
+                        const uint64_t dv =
+                            sw128_desc(sbase + L.v0 + b * L.vstage + part * 4 * kVAtom, kVAtom, 1024);
 #pragma unroll
                         for (int ks = 0; ks < kKc / 16; ++ks)
-                            umma_f16_ss(tmem + part * 256, da + ks * 2, dv + ks * (2048 >> 4),
-                                        idesc, (c > 0 || ks > 0) ? 1u : 0u);
+                            umma_f16_ss(tmem + part * 256, da + ks * 2, dv + ks * (2048 >> 4), idesc,
+                                        (c > 0 || ks > 0) ? 1u : 0u);
                     }
-                    umma_commit(bar_mma0 + 8 * b);
-                    // V buffer b is free once this MMA completes: queue chunk c+2 into it.
-                    if (c + 2 < nchunks) {
-                        mbar_wait(bar_mma0 + 8 * b, (c >> 1) & 1);
-                        load_v(c + 2);
-                    }
+                    umma_commit(bar_aempty + 8 * b);
+                    if (c == nchunks - 1) umma_commit(bar_acc);
                 }
+                __syncwarp();
+                last_issued = c;
+            }
+            // V buffer b is free once this MMA completes: queue chunk c+2 into it.
+            if (c + 2 < nchunks && warp_wait(bar_aempty + 8 * b, (c >> 1) & 1, abort)) {
+                if (lane == 0) load_v(c + 2);
                 __syncwarp();
             }
         }
-    }
-    // Epilogue: wait for the last MMA, then keep this head's hd columns.
-    const int last = nchunks - 1;
-    bool done = ok && mbar_wait(bar_mma0 + 8 * (last & 1), (last >> 1) & 1);
-    done = !__syncthreads_or(!done);
-    if (!done) {
-        if (tid == 0) atomicExch(&g_value_tc_error, 1u);
+        // Teardown: the last issued MMA completes before TMEM is released.
+        if (last_issued >= 0 &&
+            !mbar_wait(bar_aempty + 8 * (last_issued & 1), (last_issued >> 1) & 1) && lane == 0)
+            atomicExch(&g_value_tc_error, 1u);
     } else {
-        tc_fence_after();
-        const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-        T* orow = out + (static_cast<int64_t>(n) * seq + q) * channels + h * hd;
-        const int col0 = h * hd;  // first output column of this head in the C_pad block
-        for (int cb = (col0 / 32) * 32; cb < col0 + hd; cb += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_off + cb, r);
-            tmem_wait_ld();
-            reg_fence(r);
-            if (!row_live) continue;
+        // ---------------- loaders: 16 rows per warp, 4 rows per instruction ----------------
+        const int m = lane & 7;
+        int64_t ea[4];
+        int shift[4];
+        bool live[4];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int col = cb + e;
-                if (col >= col0 && col < col0 + hd) orow[col - col0] = from_f32<T>(__uint_as_float(r[e]));
+        for (int g = 0; g < 4; ++g) {
+            const int r = 16 * warp + 4 * g + (lane >> 3);
+            const int q = q0 + r;
+            live[g] = q < seq;
+            const int64_t e =
+                ((static_cast<int64_t>(n) * att_heads + ha) * seq + (live[g] ? q : 0)) * seq;
+            ea[g] = e & ~static_cast<int64_t>(7);
+            shift[g] = static_cast<int>(e - ea[g]);
+        }
+        uint4 in0[4][2], in1[4][2];
+        auto load = [&](int c, uint4 (&buf)[4][2]) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                if (live[g]) {
+                    load_piece<T>(att, ea[g] + c * kKc + 8 * m, att_elems, buf[g]);
+                } else {
+                    buf[g][0] = make_uint4(0u, 0u, 0u, 0u);
+                    buf[g][1] = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+        };
+        auto step = [&](int c, const uint4 (&buf)[4][2]) {
+            const uint32_t b = c & 1;
+            if (c >= 2) warp_wait(bar_aempty + 8 * b, ((c >> 1) - 1) & 1, abort);
+            uint8_t* tile = smem + L.a0 + b * kATile;
+            const int nk = min(kKc, seq - c * kKc);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const int r = 16 * warp + 4 * g + (lane >> 3);
+                const uint4 v =
+                    live[g] ? shift_piece(buf[g], shift[g], m, nk) : make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(tile + sw128_offset(r, m)) = v;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_afull + 8 * b);
+        };
+        load(0, in0);
+#pragma unroll 1
+        for (int c = 0; c < nchunks; c += 2) {
+            if (c + 1 < nchunks) load(c + 1, in1);
+            step(c, in0);
+            if (c + 1 < nchunks) {
+                if (c + 2 < nchunks) load(c + 2, in0);
+                step(c + 1, in1);
+            }
+        }
+        // Epilogue: warp w reads TMEM lanes 32*(w%4).. and every other 32-column block of
+        // the head's columns; only the head's hd columns are stored.
+        const int qtr = warp & 3;
+        const int r = qtr * 32 + lane;
+        const int q = q0 + r;
+        const uint32_t lane_off = static_cast<uint32_t>(qtr * 32) << 16;
+        const int off = col0 - col_base;
+        if (warp_wait(bar_acc, 0, abort)) {
+            tc_fence_after();
+            T* orow = out + (static_cast<int64_t>(n) * seq + q) * channels + col0;
+            const bool vec = off == 0 && channels % 8 == 0 && hd % 8 == 0;
+            int blk = 0;
+            for (int cb = off & ~31; cb < off + hd; cb += 32, ++blk) {
+                if ((blk & 1) != (warp >> 2)) continue;
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_off + cb, v);
+                tmem_wait_ld();
+                reg_fence(v);
+                if (q >= seq) continue;
+                if (vec && cb + 32 <= hd) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 8) {
+                        uint4 o;
+                        o.x = pack2<T>(__uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+                        o.y = pack2<T>(__uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+                        o.z = pack2<T>(__uint_as_float(v[e + 4]), __uint_as_float(v[e + 5]));
+                        o.w = pack2<T>(__uint_as_float(v[e + 6]), __uint_as_float(v[e + 7]));
+                        *reinterpret_cast<uint4*>(orow + cb + e) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const int col = cb + e - off;
+                        if (col >= 0 && col < hd) orow[col] = from_f32<T>(__uint_as_float(v[e]));
+                    }
+                }
             }
         }
     }
+
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, tcols);
+        tmem_dealloc(tmem, L.tmem_cols);
     }
 }
 
@@ -301,19 +379,20 @@ cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_
                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
         CUDA_SUCCESS)
         return cudaErrorNotSupported;
-    const Layout L = make_layout(cpad);
-    static int attr_bytes = 0;
-    if (attr_bytes < static_cast<int>(L.bytes)) {
+    static bool attr_set = false;
+    if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(zipformer_value_tc_kernel<T>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(make_layout(kMaxCpad).bytes));
         if (e != cudaSuccess) return e;
-        attr_bytes = static_cast<int>(make_layout(kMaxCpad).bytes);
+        attr_set = true;
     }
+    const Layout L = make_layout(cpad);
     const int64_t att_elems =
         static_cast<int64_t>(p.batch) * p.attention_heads * p.length * p.length;
-    const dim3 grid((p.length + kM - 1) / kM, p.value_heads, p.batch);
-    zipformer_value_tc_kernel<T><<<grid, kThreads, L.bytes, stream>>>(
+    const int64_t tiles =
+        static_cast<int64_t>(p.batch) * p.value_heads * ((p.length + kM - 1) / kM);
+    zipformer_value_tc_kernel<T><<<static_cast<unsigned int>(tiles), kThreads, L.bytes, stream>>>(
         map, static_cast<const T*>(p.attention), static_cast<T*>(p.output), p.length,
         p.attention_heads, p.value_heads, p.channels, cpad, att_elems);
     return cudaGetLastError();
@@ -323,13 +402,22 @@ cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_
 
 cudaError_t launch_zipformer_value_tc(const ZipformerValueProblem& p, cudaStream_t stream) {
     if (p.dtype != FGA_HALF && p.dtype != FGA_BF16) return cudaErrorNotSupported;
-    // TMA needs 16-byte V row strides; TMEM holds at most 512 fp32 columns.
-    if (p.channels % 8 != 0 || p.channels > kMaxCpad) return cudaErrorNotSupported;
-    if (p.batch > 65535 || p.value_heads > 65535) return cudaErrorNotSupported;
-    if ((reinterpret_cast<uintptr_t>(p.attention) & 15u) != 0 ||
-        (reinterpret_cast<uintptr_t>(p.value) & 15u) != 0)
+    // TMA needs 16-byte V row strides.
+    if (p.channels % 8 != 0 || p.value_heads < 1 || p.channels % p.value_heads != 0)
         return cudaErrorNotSupported;
-    const int cpad = (p.channels + 63) / 64 * 64;
+    // Accumulator columns: the widest head span from its first channel rounded down to 8
+    // (the offset repeats with period 8 in the head index), rounded up to 64.
+    const int hd = p.channels / p.value_heads;
+    int span = 0;
+    for (int h = 0; h < p.value_heads && h < 8; ++h) span = max(span, ((h * hd) & 7) + hd);
+    const int cpad = (span + 63) / 64 * 64;
+    if (cpad > kMaxCpad) return cudaErrorNotSupported;
+    if (static_cast<int64_t>(p.batch) * p.value_heads * ((p.length + kM - 1) / kM) > 0x7FFFFFFF)
+        return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(p.attention) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(p.value) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(p.output) & 15u) != 0)
+        return cudaErrorNotSupported;
     return p.dtype == FGA_HALF ? value_tc_typed<__half>(p, cpad, stream)
                                : value_tc_typed<__nv_bfloat16>(p, cpad, stream);
 }
