@@ -45,7 +45,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("parakeet", "zipformer"), default="parakeet")
+    p.add_argument("--workload", choices=("parakeet", "zipformer", "ragged"), default="parakeet")
     p.add_argument("--batch", type=int, default=256)
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -366,10 +366,95 @@ def workload_config(args) -> dict:
                 "frames": 375, "heads": 8, "head_dim": 128, "layers": 24,
                 "lengths": "U[60,375]", "dtype": "f16", "parallelism": f"dp{args.gpus}",
                 "l2": "inputs exceed L2 (590 MB QKV per layer, 24 distinct layers)"}
+    if args.workload == "ragged":
+        return {"workload": "ragged whole-box run (config 5): 20,000 lognormal utterances, "
+                            "length-sorted batches of 256 dealt round-robin; per batch 24 "
+                            "parakeet layers (f16) + 19 zipformer layers (bf16)",
+                "batch": args.batch, "utterances": 20000, "dtype": "f16+bf16",
+                "parallelism": f"dp{args.gpus}", "l2": "inputs exceed L2 for all but the "
+                "shortest batches; two input sets alternate per layer"}
     return {"workload": "zipformer weights + 3 attention-value calls per layer (config 3)",
             "batch": args.batch, "stacks_T": [750, 375, 188, 94, 188, 375],
             "layers": [2, 2, 4, 5, 4, 2], "dtype": "bf16", "parallelism": f"dp{args.gpus}",
             "l2": "weights tensor up to 1.15 GB per layer exceeds L2"}
+
+
+# ---- ragged whole-box run (config 5) -------------------------------------------------------
+def ragged_arm(args, world, rank, local):
+    """Length-sorted batches dealt round-robin; per batch the Parakeet stack (24 layers,
+    f16) and the Zipformer stacks (bf16); per-batch outputs gathered to rank 0 at the end.
+
+    ``value`` = audio seconds of all utterances / max over ranks of the summed kernel time
+    (CUDA events around each batch's attention calls; inputs are generated on the device
+    between batches, outside the events). The gather is timed separately.
+    """
+    import torch
+
+    from fast_gpu_asr_b200 import _lib
+    from fast_gpu_asr_b200 import workloads as wl
+    from fast_gpu_asr_b200.attention import parakeet_relative_attention
+    from fast_gpu_asr_b200.sharding import gather_to_rank0, length_sorted_batches, shard_round_robin
+
+    _lib.library()
+    stream = torch.cuda.Stream()
+    durations = wl.ragged_durations()
+    plan = length_sorted_batches(durations, args.batch)
+    mine = shard_round_robin(len(plan), world, rank)
+    kernel_ms, outputs, launches = 0.0, {}, 0
+    shapes = {}
+    for b in plan:
+        lens = np.maximum(1, np.floor(b.lengths / wl.PARAKEET_FRAME_SECONDS)).astype(np.int32)
+        shapes[b.index] = (len(lens), int(lens.max()), 1024)
+    for idx in mine:
+        b = plan[idx]
+        p_lens = np.maximum(1, np.floor(b.lengths / wl.PARAKEET_FRAME_SECONDS)).astype(np.int32)
+        t = int(p_lens.max())
+        players = [wl.make_parakeet_layer(len(p_lens), t, 8, 128, torch.float16, "cuda",
+                                          seed=7919 * idx + i, lengths=p_lens) for i in range(2)]
+        in_frames = np.maximum(2, np.round(b.lengths / wl.ZIPFORMER_INPUT_FRAME_SECONDS)).astype(np.int64)
+        stacks = []
+        for s_i, (ds, _, embed, heads, nlayers) in enumerate(wl.ZIPFORMER_STACKS):
+            lens = wl.zipformer_stack_lengths(in_frames, ds)
+            zt = int(lens.max())
+            layers = [wl.make_zipformer_layer(len(lens), zt, embed, heads, torch.bfloat16, "cuda",
+                                              7919 * idx + 100 * s_i + i, lens) for i in range(2)]
+            weights = torch.empty((len(lens), heads, zt, zt), dtype=torch.bfloat16, device="cuda")
+            outs = (torch.empty_like(layers[0].value_a), torch.empty_like(layers[0].nonlin_value))
+            stacks.append((heads, weights, [layers[i % 2] for i in range(nlayers)], outs))
+        out = torch.empty((len(p_lens), t, 1024), dtype=torch.float16, device="cuda")
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(wl.PARAKEET_LAYERS):
+                L = players[i % 2]
+                parakeet_relative_attention(L.qkv, L.position, L.content_bias, L.position_bias,
+                                            L.valid_lengths, L.scale, out=out, stream=stream)
+            run_zipformer_step(stacks, stream)
+            end.record(stream)
+        end.synchronize()
+        kernel_ms += start.elapsed_time(end)
+        launches += wl.PARAKEET_LAYERS + 4 * sum(len(s[2]) for s in stacks)
+        outputs[idx] = out
+        del players, stacks
+    barrier(world)
+    max_ms = allreduce_max(kernel_ms, world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    gathered = gather_to_rank0(outputs, shapes, world, rank, "cuda", torch.float16)
+    torch.cuda.synchronize()
+    gather_s = time.perf_counter() - t0
+    if rank == 0:
+        assert gathered is not None and len(gathered) == len(plan)
+        audio = float(durations.sum())
+        line = {"metric": METRIC, "value": audio / (max_ms / 1000.0), "unit": UNIT,
+                "n_gpus": world, "steps": 1, "warmup": 0, "ms_per_step": max_ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f16+bf16", "data": "synthetic", "config": workload_config(args),
+                "batches": len(plan), "batches_per_rank": len(mine),
+                "gather_wall_s": gather_s, "gpu_launches": launches,
+                "variant": _lib.last_kernel_variant()}
+        print(json.dumps(line), flush=True)
 
 
 # ---- our arm ---------------------------------------------------------------------------------
@@ -615,6 +700,8 @@ def main():
     try:
         if args.impl == "reference":
             reference_arm(args, world, rank)
+        elif args.workload == "ragged":
+            ragged_arm(args, world, rank, local)
         else:
             ours_arm(args, world, rank, local)
     finally:

@@ -1,0 +1,72 @@
+"""Batch sharding and the final gather (host logic; gloo world-size 2 and 3 on CPU)."""
+
+from __future__ import annotations
+
+import socket
+
+import numpy as np
+import pytest
+
+from fast_gpu_asr_b200.sharding import length_sorted_batches, shard_round_robin
+from fast_gpu_asr_b200.workloads import ragged_durations
+
+
+def test_length_sorted_batches_cover_every_utterance_once():
+    lengths = np.random.default_rng(0).integers(1, 500, size=1037)
+    plan = length_sorted_batches(lengths, 256)
+    assert [len(b.utterances) for b in plan] == [256, 256, 256, 256, 13]
+    ids = np.concatenate([b.utterances for b in plan])
+    assert sorted(ids.tolist()) == list(range(1037))
+    flat = np.concatenate([b.lengths for b in plan])
+    assert (np.diff(flat) <= 0).all()  # longest first, across batch boundaries
+    assert all((lengths[b.utterances] == b.lengths).all() for b in plan)
+
+
+def test_length_sorted_batches_is_stable_and_validates():
+    plan = length_sorted_batches([5, 7, 5, 7], 3)
+    assert plan[0].utterances.tolist() == [1, 3, 0] and plan[1].utterances.tolist() == [2]
+    with pytest.raises(ValueError):
+        length_sorted_batches([[1, 2]], 2)
+    with pytest.raises(ValueError):
+        length_sorted_batches([1, 2], 0)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_round_robin_partitions_the_plan(world):
+    n = 79  # 20,000 utterances in batches of 256
+    shards = [shard_round_robin(n, world, r) for r in range(world)]
+    flat = sorted(b for s in shards for b in s)
+    assert flat == list(range(n))
+    assert max(map(len, shards)) - min(map(len, shards)) <= 1
+    with pytest.raises(ValueError):
+        shard_round_robin(n, world, world)
+
+
+def test_ragged_box_plan_matches_the_configuration():
+    durations = ragged_durations()
+    assert durations.shape == (20000,) and durations.min() >= 1.0 and durations.max() <= 35.0
+    assert abs(durations.mean() - 8.0) < 0.3
+    assert len(length_sorted_batches(durations, 256)) == 79
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world,count,batch", [(2, 23, 4), (3, 5, 4)])
+def test_gather_to_rank0_equals_single_process(tmp_path, world, count, batch):
+    import torch.multiprocessing as mp
+
+    import dist_worker
+
+    lengths = np.random.default_rng(world).integers(3, 12, size=count).tolist()
+    out = tmp_path / "gathered.npz"
+    mp.start_processes(dist_worker.run_rank, args=(world, _free_port(), lengths, batch, str(out)),
+                       nprocs=world, join=True, start_method="spawn")
+    got = np.load(out)
+    plan = length_sorted_batches(np.asarray(lengths), batch)
+    assert sorted(int(k) for k in got.files) == [b.index for b in plan]
+    for b in plan:
+        np.testing.assert_array_equal(got[str(b.index)], dist_worker.batch_output(b.index, b.lengths))
