@@ -79,7 +79,9 @@ constexpr uint32_t kSmemV = kSmemK + kTile;
 constexpr uint32_t kSmemB0 = kSmemV + kTile;    // positional chunk slots 0 and 1
 constexpr uint32_t kSmemP = kSmemB0 + 2 * kTile;
 constexpr uint32_t kSmemXchg = kSmemP + kTile;  // [2 halves][128 rows] fp32
-constexpr uint32_t kSmemBar = kSmemXchg + 2 * kM * 4;
+constexpr uint32_t kLenCache = 256;             // valid lengths of utterances 0..255
+constexpr uint32_t kSmemLen = kSmemXchg + 2 * kM * 4;
+constexpr uint32_t kSmemBar = kSmemLen + kLenCache * 4;
 constexpr uint32_t kNumBars = 17;
 constexpr uint32_t kSmemBytes = kSmemBar + kNumBars * 8 + 16;
 
@@ -158,8 +160,18 @@ struct Item {
     int n, h, q0, valid, tiles;
 };
 
+// Valid lengths: utterances below kLenCache come from the shared-memory copy made at
+// kernel start (an item's length is on every role's critical path), the rest from global.
+struct Lengths {
+    const int32_t* __restrict__ global;
+    const int32_t* cached;
+    __device__ __forceinline__ int operator[](int n) const {
+        return n < static_cast<int>(kLenCache) ? cached[n] : __ldg(global + n);
+    }
+};
+
 __device__ __forceinline__ Item decode_item(int item, int qtiles, int heads, int length,
-                                            const int32_t* __restrict__ lengths) {
+                                            const Lengths& lengths) {
     Item it;
     const int qt = item % qtiles;
     const int nh = item / qtiles;
@@ -272,7 +284,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
 parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                    const __grid_constant__ CUtensorMap pos_map, const T* __restrict__ ubias,
-                   const T* __restrict__ vbias, const int32_t* __restrict__ lengths,
+                   const T* __restrict__ vbias, const int32_t* __restrict__ lengths_global,
                    T* __restrict__ out, int batch, int length, int heads, float scale_log2) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
@@ -293,6 +305,10 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
         if (tid == 0) atomicExch(&g_parakeet_tc_error, 2u);
         return;
     }
+    int32_t* len_cache = reinterpret_cast<int32_t*>(smem + kSmemLen);
+    for (int i = tid; i < batch && i < static_cast<int>(kLenCache); i += kThreads)
+        len_cache[i] = lengths_global[i];
+    const Lengths lengths{lengths_global, len_cache};
     if (tid == 0) {
         for (uint32_t i = 0; i < kNumBars; ++i) {
             const bool per_warp = i == kBarQReady || i == kBarSFree || i == kBarPFull ||
@@ -488,18 +504,15 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
             const Item it = decode_item(item, qtiles, heads, length, lengths);
             // The candidate's length load is issued now and consumed at the last tile.
             const int cand = item + gridDim.x;
-            const int cand_len = cand < num_items ? __ldg(lengths + cand / (qtiles * heads)) : 0;
+            const int cand_len = cand < num_items ? lengths[cand / (qtiles * heads)] : 0;
             int next = num_items;
             for (int j = 0; j < it.tiles && ok; ++j) {
                 if (j + 1 == it.tiles && cand < num_items)
                     next = cand_len > 0 ? cand : next_item(cand);
-                // Keep the tensor pipe fed: the next tile's (or next item's) score
-                // MMAs go ahead of this tile's P.V.
-                if (j + 1 < it.tiles) {
-                    if (!(ok = issue_s(false, j + 2 == it.tiles))) break;
-                } else if (next < num_items) {
-                    if (!(ok = start_item(next))) break;
-                }
+                // Keep the tensor pipe fed: the next tile's score MMAs go ahead of this
+                // tile's P.V. (The next item's first score MMAs follow the last P.V: its
+                // biased queries are formed while that P.V runs.)
+                if (j + 1 < it.tiles && !(ok = issue_s(false, j + 2 == it.tiles))) break;
                 if (!(ok = wait(kBarPFull, v_iter & 1))) break;
                 if (!(ok = wait(kBarVFull, v_iter & 1))) break;
                 if (j == 0 && items_done > 0 && !(ok = wait(kBarOFree, (items_done - 1) & 1)))
@@ -516,6 +529,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 }
                 __syncwarp();
                 ++v_iter;
+                if (j + 1 == it.tiles && next < num_items && !(ok = start_item(next))) break;
             }
             ++items_done;
             item = next;
@@ -571,7 +585,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
             const Item it = decode_item(item, qtiles, heads, length, lengths);
             // The candidate's length load is issued now and consumed at the last tile.
             const int cand = item + gridDim.x;
-            const int cand_len = cand < num_items ? __ldg(lengths + cand / (qtiles * heads)) : 0;
+            const int cand_len = cand < num_items ? lengths[cand / (qtiles * heads)] : 0;
             int next = num_items;
             float m_run = -INFINITY;  // reference max (base-2 logits)
             float l_run = 0.0f;       // this half's running sum of 2^(logit - m_run)
@@ -591,12 +605,6 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(sync.bar(kBarSFree));
-                // After the last tile's scores, prepare the next item's queries so its
-                // first MMAs run under this item's exponentials and epilogue.
-                if (j + 1 == it.tiles && cand < num_items) {
-                    next = cand_len > 0 ? cand : next_item(cand);
-                    if (next < num_items && !(ok = prepare_queries(next))) break;
-                }
 
                 const float m_half = tree_max(s);
                 xchg[half * kM + row] = m_half;
@@ -650,6 +658,12 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(sync.bar(kBarPFull));
+                // After the last tile's P, prepare the next item's queries while the
+                // last P.V runs; its first score MMAs then run under this epilogue.
+                if (j + 1 == it.tiles && cand < num_items) {
+                    next = cand_len > 0 ? cand : next_item(cand);
+                    if (next < num_items && !(ok = prepare_queries(next))) break;
+                }
             }
             if (!ok) break;
             h_base += it.tiles + 1;
