@@ -265,6 +265,21 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr, uint32_t lbo_
     return d;
 }
 
+// Shared-memory matrix descriptor for any canonical layout: `layout` is the layout-type
+// field (0 none, 2 SWIZZLE_128B, 4 SWIZZLE_64B, 6 SWIZZLE_32B); for MN-major swizzled
+// operands LBO is the stride between swizzle atoms along M/N and SBO between 8-row groups
+// along K.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint32_t layout) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;
+    d |= static_cast<uint64_t>(layout & 7u) << 61;
+    return d;
+}
+
 // Instruction descriptor for kind::f16 with f32 accumulation.
 // ab_format: 0 = f16, 1 = bf16. a_mn_major / b_mn_major: 0 = K-major, 1 = MN-major.
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_format, uint32_t m, uint32_t n,

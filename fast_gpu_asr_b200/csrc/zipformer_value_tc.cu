@@ -21,11 +21,17 @@
 //               tile writes are bank-conflict free).
 //   warps 7-10  epilogue: after the last chunk of a tile, read the accumulator from TMEM
 //               and store the head's output columns, while the next tile streams in.
-//   warp 5      MMA issuer; warp 6 V producer. V arrives by TMA as MN-major SWIZZLE_128B
-//               tiles of 64 channels starting at the head's first channel (rounded down
-//               to 8), so a self-attention head (12 channels) needs one 64-wide tile and
-//               the NonlinAttention value (3E/4 channels, head 0) ceil(C/64) of them.
-//               Accumulators (fp32, TMEM) are double-buffered across tiles when they fit.
+//   warp 5      MMA issuer; warp 6 V producer. A V tile holds the chunk's 64 keys of the
+//               channels from the head's first channel (rounded down to 8) in MN-major
+//               swizzled atoms, as narrow as the head allows: a self-attention head (12
+//               channels) is one 16-channel SWIZZLE_32B atom (2 KB per chunk) and an N = 16
+//               MMA. Tiles up to 64 channels wide are copied by the V warp with 16-byte
+//               cp.async straight into their swizzled slots, several chunks ahead, so V
+//               takes no place in the SM's TMA queue: there every V key would be one box row
+//               (64 per chunk, more than the A boxes' 43), and the A stream would wait
+//               behind them. Wider tiles (the NonlinAttention value, 3E/4 channels of head
+//               0) arrive by TMA in ceil(C/64) 64-channel SWIZZLE_128B atoms. Accumulators
+//               (fp32, TMEM) are double-buffered across tiles when they fit.
 //
 // All waits are bounded; a timeout raises the CTA's abort word, after which every role
 // skips its work but keeps its loop, so nothing waits on a role that has stopped.
@@ -54,8 +60,10 @@ __host__ __device__ constexpr uint32_t raw_row_bytes(int sup) { return (64u * su
 __host__ __device__ constexpr uint32_t raw_stage_bytes(int sup) { return 128u * raw_row_bytes(sup); }
 constexpr uint32_t kSbo = 1040;               // 8-row core-matrix groups (16 mod 128)
 constexpr uint32_t kATile = 16 * kSbo;        // 128 rows x 64 keys, no swizzle
-constexpr uint32_t kVAtom = kKc * 128;        // 8 KB: 64 keys x 64 channels
 constexpr uint32_t kSmemLimit = 227 * 1024;
+constexpr uint32_t kMaxVStages = 8;   // streaming V ring
+constexpr uint32_t kMaxVRes = 16;     // resident V: chunks per row (keys <= 1024)
+constexpr uint32_t kBarBytes = 512;
 
 __device__ unsigned int g_value_tc_error = 0;
 
@@ -74,53 +82,73 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
 }
 
 struct Layout {
-    uint32_t sup, raw_row, raw_stage, raw_stages, v_stages, acc_bufs;
-    uint32_t raw0, a0, v0, vstage, bar, bytes, tmem_cols;
+    uint32_t sup, raw_row, raw_stage, raw_stages, a_tiles, v_stages, acc_bufs, acc_stride;
+    uint32_t vw, vatom, vstage;  // V atom width (channels) and bytes; bytes per V stage
+    uint32_t vres;               // 1: one V stage per chunk, loaded once per (n, h) run
+    uint32_t raw0, a0, v0, bar, bytes, tmem_cols;
 };
 
 __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
     return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
 }
 
-// Shared-memory plan for `cpad` accumulator columns: narrow V tiles (cpad <= 128) get
-// 3-chunk super-chunks in a 3-deep raw ring; wide ones single chunks in a 4-deep ring
-// (2 when needed); then two A tiles and up to 4 V stages in what is left.
-__host__ __device__ constexpr Layout make_layout(int cpad) {
+// Shared-memory plan for `cpad` accumulator columns (16, 32 or a multiple of 64) and
+// rows of `seq` keys. A V atom is 64 keys x vw channels (vw = cpad up to 64): rows of
+// 2*vw bytes, swizzled over 2*vw bytes (SWIZZLE_32B, 64B or 128B). Narrow V tiles
+// (cpad <= 128) get 3-chunk super-chunks in a 3-deep raw ring, wide ones single chunks in
+// a 4-deep raw ring; two A tiles. When a V stage per chunk of the whole row fits (at most
+// kMaxVRes chunks), V is resident: each chunk's stage is loaded once per run of tiles of
+// one (utterance, head) and serves all its query blocks. Otherwise up to kMaxVStages V
+// stages stream; while fewer than 2 fit, the raw ring gives up stages.
+__host__ __device__ constexpr Layout make_layout(int cpad, int seq) {
     Layout l{};
-    l.vstage = static_cast<uint32_t>(cpad / 64) * kVAtom;
-    l.sup = cpad <= 128 ? 3 : 1;
+    l.vw = cpad < 64 ? static_cast<uint32_t>(cpad) : 64u;
+    l.vatom = static_cast<uint32_t>(kKc) * l.vw * 2u;
+    l.vstage = (static_cast<uint32_t>(cpad) / l.vw) * l.vatom;
+    const bool narrow = cpad <= 128;
+    l.sup = narrow ? 3u : 1u;
     l.raw_row = raw_row_bytes(static_cast<int>(l.sup));
     l.raw_stage = raw_stage_bytes(static_cast<int>(l.sup));
-    l.raw_stages = l.sup == 3 ? 3 : 4;
-    uint32_t fixed = l.raw_stages * l.raw_stage + 2 * kATile + 1024 + 256;
-    l.v_stages = (kSmemLimit - fixed) / l.vstage;
-    if (l.v_stages < 2) {
-        l.raw_stages = 2;
-        fixed = l.raw_stages * l.raw_stage + 2 * kATile + 1024 + 256;
-        l.v_stages = (kSmemLimit - fixed) / l.vstage;
+    l.raw_stages = narrow ? 3u : 4u;
+    l.a_tiles = 2;
+    const uint32_t nchunks = static_cast<uint32_t>((seq + kKc - 1) / kKc);
+    uint32_t fixed = l.raw_stages * l.raw_stage + l.a_tiles * kATile + 1024 + kBarBytes;
+    if (nchunks <= kMaxVRes && fixed + nchunks * l.vstage <= kSmemLimit) {
+        l.vres = 1;
+        l.v_stages = nchunks;
+    } else {
+        for (;;) {
+            l.v_stages = fixed < kSmemLimit ? (kSmemLimit - fixed) / l.vstage : 0u;
+            if (l.v_stages >= 2 || l.raw_stages == 2) break;
+            --l.raw_stages;
+            fixed = l.raw_stages * l.raw_stage + l.a_tiles * kATile + 1024 + kBarBytes;
+        }
+        if (l.v_stages > kMaxVStages) l.v_stages = kMaxVStages;
     }
-    if (l.v_stages > 4) l.v_stages = 4;
-    l.acc_bufs = 2 * cpad <= kMaxCpad ? 2 : 1;
+    // The epilogue reads 32 accumulator columns at a time.
+    l.acc_stride = cpad < 32 ? 32u : static_cast<uint32_t>(cpad);
+    l.acc_bufs = 2 * l.acc_stride <= kMaxCpad ? 2 : 1;
     l.raw0 = 0;
     l.a0 = l.raw_stages * l.raw_stage;
-    l.v0 = (l.a0 + 2 * kATile + 1023u) & ~1023u;  // SWIZZLE_128B atoms: 1024-byte aligned
+    l.v0 = (l.a0 + l.a_tiles * kATile + 1023u) & ~1023u;  // swizzle atoms: 1024-byte aligned
     l.bar = l.v0 + l.v_stages * l.vstage;
-    l.bytes = l.bar + 256;
-    l.tmem_cols = pow2_cols(l.acc_bufs * cpad);
+    l.bytes = l.bar + kBarBytes;
+    l.tmem_cols = pow2_cols(l.acc_bufs * l.acc_stride);
     return l;
 }
 
-struct Bars {  // mbarrier addresses (shared window)
+struct Bars {  // mbarrier addresses (shared window); the TMEM slot and abort word follow
     uint32_t base;
-    __device__ uint32_t raw_full(uint32_t s) const { return base + 8 * s; }
-    __device__ uint32_t raw_empty(uint32_t s) const { return base + 32 + 8 * s; }
-    __device__ uint32_t a_full(uint32_t t) const { return base + 64 + 8 * t; }
-    __device__ uint32_t a_empty(uint32_t t) const { return base + 80 + 8 * t; }
-    __device__ uint32_t v_full(uint32_t s) const { return base + 96 + 8 * s; }
-    __device__ uint32_t v_empty(uint32_t s) const { return base + 128 + 8 * s; }
-    __device__ uint32_t acc_full(uint32_t b) const { return base + 160 + 8 * b; }
-    __device__ uint32_t acc_empty(uint32_t b) const { return base + 176 + 8 * b; }
+    __device__ uint32_t raw_full(uint32_t s) const { return base + 8 * s; }        // <= 5
+    __device__ uint32_t raw_empty(uint32_t s) const { return base + 40 + 8 * s; }
+    __device__ uint32_t a_full(uint32_t t) const { return base + 80 + 8 * t; }         // <= 4
+    __device__ uint32_t a_empty(uint32_t t) const { return base + 112 + 8 * t; }
+    __device__ uint32_t acc_full(uint32_t b) const { return base + 144 + 8 * b; }      // <= 2
+    __device__ uint32_t acc_empty(uint32_t b) const { return base + 160 + 8 * b; }
+    __device__ uint32_t v_full(uint32_t s) const { return base + 176 + 8 * s; }        // <= 16
+    __device__ uint32_t v_empty(uint32_t s) const { return base + 304 + 8 * s; }
 };
+constexpr uint32_t kTmemSlotOff = 432, kAbortOff = 436;
 
 // Bounded wait with a warp-uniform result; a failure raises the CTA's abort word.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
@@ -153,24 +181,37 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t smem_addr) {
     return d;
 }
 
-// Byte offset of 16-byte chunk cc (8 keys) of row j in the A tile.
-__device__ __forceinline__ uint32_t a_offset(int j, int cc) {
-    return static_cast<uint32_t>(j >> 3) * kSbo + static_cast<uint32_t>(cc) * 128u +
-           static_cast<uint32_t>(j & 7) * 16u;
-}
-
-struct TileInfo {
-    int n, h, q0;
+// Walks a CTA's contiguous range of tiles; tile = (n * heads + h) * nqb + qb, so the query
+// blocks of one (utterance, head) are consecutive.
+struct TileCursor {
+    int qb, h, n;
+    __device__ void init(int tile, int heads, int nqb) {
+        qb = tile % nqb;
+        const int nh = tile / nqb;
+        h = nh % heads;
+        n = nh / heads;
+    }
+    __device__ void next(int heads, int nqb) {
+        if (++qb == nqb) {
+            qb = 0;
+            if (++h == heads) {
+                h = 0;
+                ++n;
+            }
+        }
+    }
 };
 
-__device__ __forceinline__ TileInfo tile_info(int tile, int heads, int nqb) {
-    TileInfo t;
-    t.q0 = (tile % nqb) * kM;
-    const int nh = tile / nqb;
-    t.h = nh % heads;
-    t.n = nh / heads;
-    return t;
-}
+// Ring position: slot and the parity of its current phase.
+struct Ring {
+    uint32_t slot = 0, phase = 0;
+    __device__ void next(uint32_t n) {
+        if (++slot == n) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -180,10 +221,10 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
                           int num_tiles) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
-    const Layout L = make_layout(cpad);
+    const Layout L = make_layout(cpad, seq);
     const Bars B{sbase + L.bar};
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + 192);
-    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + L.bar + 196);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.bar + kTmemSlotOff);
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + L.bar + kAbortOff);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -191,8 +232,12 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
     const int hd = channels / value_heads;
     const int nqb = (seq + kM - 1) / kM;
     const int nchunks = (seq + kKc - 1) / kKc;
-    const int my_tiles = (num_tiles - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1;
-    const int total = my_tiles * nchunks;
+    const int sup = static_cast<int>(L.sup);
+    const int nsup = (nchunks + sup - 1) / sup;
+    // A contiguous, balanced range of tiles per CTA (grid <= tiles, so none is empty).
+    const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * num_tiles / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * num_tiles / gridDim.x);
+    const int my_tiles = t_end - t_begin;
 
     if ((sbase & 1023u) != 0) {
         if (tid == 0) atomicExch(&g_value_tc_error, 2u);
@@ -203,11 +248,13 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
             mbar_init(B.raw_full(s), 1);
             mbar_init(B.raw_empty(s), 4);
         }
-        for (uint32_t t = 0; t < 2; ++t) {
+        for (uint32_t t = 0; t < L.a_tiles; ++t) {
             mbar_init(B.a_full(t), 4);
             mbar_init(B.a_empty(t), 1);
-            mbar_init(B.acc_full(t), 1);
-            mbar_init(B.acc_empty(t), 4);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(B.acc_full(b), 1);
+            mbar_init(B.acc_empty(b), 4);
         }
         for (uint32_t s = 0; s < L.v_stages; ++s) {
             mbar_init(B.v_full(s), 1);
@@ -227,108 +274,149 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    const int nsup = (nchunks + static_cast<int>(L.sup) - 1) / static_cast<int>(L.sup);
-    const int total_sup = my_tiles * nsup;
     if (warp == 0) {
         // ---------------- A producer: one super-chunk per raw stage ----------------
+        TileCursor cur;
+        cur.init(t_begin, value_heads, nqb);
+        Ring rs;
+        int gs = 0;
 #pragma unroll 1
-        for (int gs = 0; gs < total_sup; ++gs) {
-            const int i = gs / nsup, sc = gs - i * nsup;
-            const TileInfo ti = tile_info(blockIdx.x + i * gridDim.x, value_heads, nqb);
-            const int ha = value_heads == 1 ? 0 : ti.h;
-            const uint32_t s = gs % L.raw_stages;
-            if (gs >= static_cast<int>(L.raw_stages) &&
-                !warp_wait(B.raw_empty(s), ((gs / L.raw_stages) - 1) & 1, abort))
-                continue;
-            if (__any_sync(0xffffffffu, *abort != 0u)) continue;
-            // Rows j = slot + 8i (i < 16) of the tile form one box of class (R0+slot) mod 8.
-            if (lane < 8) {
-                const int64_t R = (static_cast<int64_t>(ti.n) * att_heads + ha) * seq + ti.q0 + lane;
-                if (lane == 0) mbar_expect_tx(B.raw_full(s), L.raw_stage);
-                __syncwarp(0xffu);
-                tma_load_2d(sbase + L.raw0 + s * L.raw_stage + lane * 16 * L.raw_row,
-                            &a_maps.m[R & 7], B.raw_full(s), sc * kKc * static_cast<int>(L.sup),
-                            static_cast<int32_t>(R >> 3));
-            }
-            __syncwarp();
-        }
-    } else if (warp == 6) {
-        // ---------------- V producer: up to v_stages chunks ahead of the MMAs ----------------
+        for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
+            const int ha = value_heads == 1 ? 0 : cur.h;
+            // Rows j = slot + 8m (m < 16) of the tile form one box of class (R0+slot) mod 8.
+            const int64_t R = (static_cast<int64_t>(cur.n) * att_heads + ha) * seq + cur.qb * kM + lane;
 #pragma unroll 1
-        for (int g = 0; g < total; ++g) {
-            const int i = g / nchunks, c = g - i * nchunks;
-            const uint32_t vs = g % L.v_stages;
-            if (g >= static_cast<int>(L.v_stages) &&
-                !warp_wait(B.v_empty(vs), ((g / L.v_stages) - 1) & 1, abort))
-                continue;
-            if (lane == 0) {
-                const TileInfo ti = tile_info(blockIdx.x + i * gridDim.x, value_heads, nqb);
-                const int col_base = (ti.h * hd) & ~7;
-                mbar_expect_tx(B.v_full(vs), L.vstage);
-                for (int x = 0; x < cpad / 64; ++x)
-                    tma_load_3d(sbase + L.v0 + vs * L.vstage + x * kVAtom, &v_map, B.v_full(vs),
-                                col_base + x * 64, c * kKc, ti.n);
-            }
-            __syncwarp();
-        }
-    } else if (warp == 5) {
-        // ---------------- MMA issuer ----------------
-        const uint32_t idesc_base = idesc_f16(Fmt<T>::v, kM, 16, 0, 1);  // N patched per part
-#pragma unroll 1
-        for (int gc = 0; gc < total; ++gc) {
-            const int i = gc / nchunks, c = gc - i * nchunks;
-            const uint32_t t = gc & 1, vs = gc % L.v_stages, b = i % L.acc_bufs;
-            bool ok = warp_wait(B.a_full(t), (gc >> 1) & 1, abort);
-            ok = ok && warp_wait(B.v_full(vs), (gc / L.v_stages) & 1, abort);
-            if (ok && c == 0 && i >= static_cast<int>(L.acc_bufs))
-                ok = warp_wait(B.acc_empty(b), ((i / L.acc_bufs) - 1) & 1, abort);
-            if (ok) {
-                tc_fence_after();
-                if (elect_one()) {
-                    const uint64_t da = kmajor_desc(sbase + L.a0 + t * kATile);
-                    for (int part = 0; part * 256 < cpad; ++part) {
-                        const int nw = min(256, cpad - part * 256);
-                        const uint32_t idesc = idesc_base + ((static_cast<uint32_t>(nw) >> 3) << 17) -
-                                               ((16u >> 3) << 17);
-                        // V: MN-major, 64-channel atoms kVAtom bytes apart, 16 keys = 2048 B.
-                        const uint64_t dv = sw128_desc(
-                            sbase + L.v0 + vs * L.vstage + part * 4 * kVAtom, kVAtom, 1024);
-#pragma unroll
-                        for (int ks = 0; ks < kKc / 16; ++ks)
-                            umma_f16_ss(tmem + b * cpad + part * 256, da + ks * (256 >> 4),
-                                        dv + ks * (2048 >> 4), idesc, (c > 0 || ks > 0) ? 1u : 0u);
-                    }
-                    umma_commit(B.a_empty(t));
-                    umma_commit(B.v_empty(vs));
-                    if (c == nchunks - 1) umma_commit(B.acc_full(b));
+            for (int sc = 0; sc < nsup; ++sc, ++gs, rs.next(L.raw_stages)) {
+                if (gs >= static_cast<int>(L.raw_stages) &&
+                    !warp_wait(B.raw_empty(rs.slot), rs.phase ^ 1u, abort))
+                    continue;
+                if (__any_sync(0xffffffffu, *abort != 0u)) continue;
+                if (lane < 8) {
+                    if (lane == 0) mbar_expect_tx(B.raw_full(rs.slot), L.raw_stage);
+                    __syncwarp(0xffu);
+                    tma_load_2d(sbase + L.raw0 + rs.slot * L.raw_stage + lane * 16 * L.raw_row,
+                                &a_maps.m[R & 7], B.raw_full(rs.slot), sc * kKc * sup,
+                                static_cast<int32_t>(R >> 3));
                 }
                 __syncwarp();
             }
         }
-        // Teardown: every MMA of this CTA completes before TMEM is released.
-        if (total > 0) {
-            const int last = total - 1;
-            if (!mbar_wait(B.a_empty(last & 1), (last >> 1) & 1) && lane == 0)
-                atomicExch(&g_value_tc_error, 1u);
+    } else if (warp == 6) {
+        // ---------------- V producer ----------------
+        // Resident: at the start of each run of tiles of one (n, h), chunk c's stage c is
+        // reloaded once the MMAs of the previous run's last tile have released it.
+        // Streaming: one stage per chunk of every tile, up to v_stages ahead of the MMAs.
+        TileCursor cur;
+        cur.init(t_begin, value_heads, nqb);
+        Ring vr;
+        int run = 0, g = 0;
+#pragma unroll 1
+        for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
+            const bool run_start = i == 0 || cur.qb == 0;
+            if (L.vres && !run_start) continue;
+            const int col_base = (cur.h * hd) & ~7;
+#pragma unroll 1
+            for (int c = 0; c < nchunks; ++c, ++g) {
+                uint32_t vs;
+                bool ok;
+                if (L.vres) {
+                    vs = static_cast<uint32_t>(c);
+                    ok = run == 0 || warp_wait(B.v_empty(vs), (run - 1) & 1, abort);
+                } else {
+                    vs = vr.slot;
+                    ok = g < static_cast<int>(L.v_stages) ||
+                         warp_wait(B.v_empty(vs), vr.phase ^ 1u, abort);
+                    vr.next(L.v_stages);
+                }
+                if (ok && lane == 0) {
+                    mbar_expect_tx(B.v_full(vs), L.vstage);
+                    for (int x = 0; x < cpad / static_cast<int>(L.vw); ++x)
+                        tma_load_3d(sbase + L.v0 + vs * L.vstage + x * L.vatom, &v_map,
+                                    B.v_full(vs), col_base + x * static_cast<int>(L.vw), c * kKc,
+                                    cur.n);
+                }
+                __syncwarp();
+            }
+            ++run;
         }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        // V: MN-major atoms of vw channels, vatom bytes apart along N; 8-key groups of
+        // 16*vw bytes; one 16-key step = 32*vw bytes. Descriptor start addresses advance in
+        // 16-byte units.
+        const uint32_t vlayout = L.vw == 16 ? 6u : L.vw == 32 ? 4u : 2u;  // SWIZZLE_32B/64B/128B
+        const uint64_t da0 = kmajor_desc(sbase + L.a0);
+        const uint64_t dv0 = smem_desc(sbase + L.v0, L.vatom, 16 * L.vw, vlayout);
+        const uint32_t part_atoms = (256u / L.vw) * L.vatom;
+        const uint32_t idesc_full = idesc_f16(Fmt<T>::v, kM, 256, 0, 1);
+        const uint32_t idesc_last = idesc_f16(Fmt<T>::v, kM, ((cpad - 1) & 255) + 1, 0, 1);
+        const int parts = (cpad + 255) / 256;
+        TileCursor cur;
+        cur.init(t_begin, value_heads, nqb);
+        Ring ar, vr, acc;
+        int run = -1;
+        uint32_t last_slot = 0, last_phase = 0;
+#pragma unroll 1
+        for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
+            if (i == 0 || cur.qb == 0) ++run;
+            const bool run_end = i + 1 == my_tiles || cur.qb == nqb - 1;
+            bool tile_ok = true;
+            if (i >= static_cast<int>(L.acc_bufs))
+                tile_ok = warp_wait(B.acc_empty(acc.slot), acc.phase ^ 1u, abort);
+            const uint32_t d_acc = tmem + acc.slot * L.acc_stride;
+#pragma unroll 1
+            for (int c = 0; c < nchunks; ++c, ar.next(L.a_tiles)) {
+                const uint32_t vs = L.vres ? static_cast<uint32_t>(c) : vr.slot;
+                const uint32_t vph = L.vres ? static_cast<uint32_t>(run & 1) : vr.phase;
+                if (!L.vres) vr.next(L.v_stages);
+                bool ok = tile_ok && warp_wait(B.a_full(ar.slot), ar.phase, abort);
+                ok = ok && warp_wait(B.v_full(vs), vph, abort);
+                last_slot = ar.slot;
+                last_phase = ar.phase;
+                if (!ok) continue;
+                tc_fence_after();
+                if (elect_one()) {
+                    const uint64_t da = da0 + ar.slot * (kATile >> 4);
+                    const uint64_t dv = dv0 + ((vs * L.vstage) >> 4);
+                    for (int part = 0; part < parts; ++part) {
+                        const uint32_t idesc = part + 1 == parts ? idesc_last : idesc_full;
+#pragma unroll
+                        for (int ks = 0; ks < kKc / 16; ++ks)
+                            umma_f16_ss(d_acc + part * 256, da + ks * (256 >> 4),
+                                        dv + ((part * part_atoms + ks * 32 * L.vw) >> 4), idesc,
+                                        (c > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    umma_commit(B.a_empty(ar.slot));
+                    if (!L.vres || run_end) umma_commit(B.v_empty(vs));
+                    if (c == nchunks - 1) umma_commit(B.acc_full(acc.slot));
+                }
+                __syncwarp();
+            }
+            acc.next(L.acc_bufs);
+        }
+        // Teardown: every MMA of this CTA completes before TMEM is released.
+        if (!mbar_wait(B.a_empty(last_slot), last_phase) && lane == 0)
+            atomicExch(&g_value_tc_error, 1u);
     } else if (warp >= 7) {
         // ---------------- epilogue warps 7..10 ----------------
         const int qtr = warp & 3;
         const int r = qtr * 32 + lane;  // output row = TMEM lane
         const uint32_t lane_off = static_cast<uint32_t>(qtr * 32) << 16;
-        auto epilogue = [&](int i) {
-            const TileInfo ti = tile_info(blockIdx.x + i * gridDim.x, value_heads, nqb);
-            const uint32_t b = i % L.acc_bufs;
-            if (warp_wait(B.acc_full(b), (i / L.acc_bufs) & 1, abort)) {
+        TileCursor cur;
+        cur.init(t_begin, value_heads, nqb);
+        Ring acc;
+#pragma unroll 1
+        for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb), acc.next(L.acc_bufs)) {
+            if (warp_wait(B.acc_full(acc.slot), acc.phase, abort)) {
                 tc_fence_after();
-                const int q = ti.q0 + r;
-                const int col0 = ti.h * hd;
+                const int q = cur.qb * kM + r;
+                const int col0 = cur.h * hd;
                 const int off = col0 & 7;  // first head column inside the V tile
-                T* orow = out + (static_cast<int64_t>(ti.n) * seq + q) * channels + col0;
+                T* orow = out + (static_cast<int64_t>(cur.n) * seq + q) * channels + col0;
                 const bool vec = off == 0 && channels % 8 == 0 && hd % 8 == 0;
                 for (int cb = off & ~31; cb < off + hd; cb += 32) {
                     uint32_t v[32];
-                    tmem_ld32(tmem + lane_off + b * cpad + cb, v);
+                    tmem_ld32(tmem + lane_off + acc.slot * L.acc_stride + cb, v);
                     tmem_wait_ld();
                     reg_fence(v);
                     if (q >= seq) continue;
@@ -353,87 +441,86 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(B.acc_empty(b));
-        };
-#pragma unroll 1
-        for (int i = 0; i < my_tiles; ++i) epilogue(i);
+            if (lane == 0) mbar_arrive(B.acc_empty(acc.slot));
+        }
     } else {
         // ---------------- repack warps 1..4 ----------------
-        // Repack row: thread t = 16 * slot + i handles row j = slot + 8i, so that the 8
+        // Repack row: thread t = 16 * slot + m handles row j = slot + 8m, so that the 8
         // lanes of a shared-memory phase read 8 consecutive box rows of one class and
         // write 8 consecutive core-matrix groups.
         const int rt = (warp - 1) * 32 + lane;
         const int slot = rt >> 4, bi = rt & 15;
         const int j = slot + 8 * bi;
+        const uint32_t a_row = static_cast<uint32_t>(j >> 3) * kSbo + static_cast<uint32_t>(j & 7) * 16u;
+        TileCursor cur;
+        cur.init(t_begin, value_heads, nqb);
+        Ring rs, ar;
         int gc = 0;
 #pragma unroll 1
-        for (int gs = 0; gs < total_sup; ++gs) {
-            const int i = gs / nsup, sc = gs - i * nsup;
-            const TileInfo ti = tile_info(blockIdx.x + i * gridDim.x, value_heads, nqb);
-            const int ha = value_heads == 1 ? 0 : ti.h;
-            const uint32_t s = gs % L.raw_stages;
-            const bool raw_ok = warp_wait(B.raw_full(s), (gs / L.raw_stages) & 1, abort);
-            const int c_end = min(nchunks, (sc + 1) * static_cast<int>(L.sup));
+        for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
+            const int ha = value_heads == 1 ? 0 : cur.h;
+            const int q = cur.qb * kM + j;
+            const int64_t R = (static_cast<int64_t>(cur.n) * att_heads + ha) * seq + q;
+            const int a = class_offset(static_cast<int>(R & 7), seq);
+            // Shift by a elements: whole words (a >> 1) with a predicated barrel, then half a
+            // word with a funnel shift.
+            const uint32_t sw = static_cast<uint32_t>(a) >> 1;
+            const uint32_t sh = (a & 1) ? 16u : 0u;
+            int c = 0;
 #pragma unroll 1
-            for (int c = sc * static_cast<int>(L.sup); c < c_end; ++c, ++gc) {
-                const int sub = c - sc * static_cast<int>(L.sup);
-                const uint32_t t = gc & 1;
-                bool ok = raw_ok;
-                if (ok && gc >= 2) ok = warp_wait(B.a_empty(t), ((gc >> 1) - 1) & 1, abort);
-                if (ok) {
-                    const int q = ti.q0 + j;
-                    const int k0 = c * kKc;
-                    const int nk = min(kKc, seq - k0);
-                    uint32_t w[36];
-                    if (q < seq) {
-                        const int64_t R0 =
-                            (static_cast<int64_t>(ti.n) * att_heads + ha) * seq + ti.q0;
-                        const int a = class_offset(static_cast<int>((R0 + slot) & 7), seq);
-                        const uint4* raw = reinterpret_cast<const uint4*>(
-                            smem + L.raw0 + s * L.raw_stage + (slot * 16 + bi) * L.raw_row +
-                            sub * 128);
+            for (int sc = 0; sc < nsup; ++sc, rs.next(L.raw_stages)) {
+                const bool raw_ok = warp_wait(B.raw_full(rs.slot), rs.phase, abort);
+                const uint8_t* raw_row =
+                    smem + L.raw0 + rs.slot * L.raw_stage + (slot * 16 + bi) * L.raw_row;
+#pragma unroll 1
+                for (int sub = 0; sub < sup && c < nchunks; ++sub, ++c, ++gc, ar.next(L.a_tiles)) {
+                    bool ok = raw_ok;
+                    if (ok && gc >= static_cast<int>(L.a_tiles))
+                        ok = warp_wait(B.a_empty(ar.slot), ar.phase ^ 1u, abort);
+                    if (ok) {
+                        const int nk = min(kKc, seq - c * kKc);
+                        uint32_t w[36];
+                        if (q < seq) {
+                            const uint4* src = reinterpret_cast<const uint4*>(raw_row + sub * 128);
 #pragma unroll
-                        for (int x = 0; x < 9; ++x) {
-                            const uint4 v = raw[x];
-                            w[4 * x] = v.x;
-                            w[4 * x + 1] = v.y;
-                            w[4 * x + 2] = v.z;
-                            w[4 * x + 3] = v.w;
-                        }
-                        // Shift by a elements: whole words (a >> 1) with a predicated
-                        // barrel, then half a word with a funnel shift.
-                        const uint32_t sw = static_cast<uint32_t>(a) >> 1;
-#pragma unroll
-                        for (int x = 0; x < 34; ++x) w[x] = (sw & 2u) ? w[x + 2] : w[x];
-#pragma unroll
-                        for (int x = 0; x < 33; ++x) w[x] = (sw & 1u) ? w[x + 1] : w[x];
-                        const uint32_t sh = (a & 1) ? 16u : 0u;
-#pragma unroll
-                        for (int x = 0; x < 32; ++x) w[x] = __funnelshift_r(w[x], w[x + 1], sh);
-                        if (nk < kKc) {
-#pragma unroll
-                            for (int x = 0; x < 32; ++x) {
-                                const int k = 2 * x;
-                                if (k >= nk) w[x] = 0u;
-                                else if (k + 1 >= nk) w[x] &= 0xFFFFu;
+                            for (int x = 0; x < 9; ++x) {
+                                const uint4 v = src[x];
+                                w[4 * x] = v.x;
+                                w[4 * x + 1] = v.y;
+                                w[4 * x + 2] = v.z;
+                                w[4 * x + 3] = v.w;
                             }
+#pragma unroll
+                            for (int x = 0; x < 34; ++x) w[x] = (sw & 2u) ? w[x + 2] : w[x];
+#pragma unroll
+                            for (int x = 0; x < 33; ++x) w[x] = (sw & 1u) ? w[x + 1] : w[x];
+#pragma unroll
+                            for (int x = 0; x < 32; ++x) w[x] = __funnelshift_r(w[x], w[x + 1], sh);
+                            if (nk < kKc) {
+#pragma unroll
+                                for (int x = 0; x < 32; ++x) {
+                                    const int k = 2 * x;
+                                    if (k >= nk) w[x] = 0u;
+                                    else if (k + 1 >= nk) w[x] &= 0xFFFFu;
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int x = 0; x < 32; ++x) w[x] = 0u;
                         }
-                    } else {
+                        uint8_t* tile = smem + L.a0 + ar.slot * kATile + a_row;
 #pragma unroll
-                        for (int x = 0; x < 32; ++x) w[x] = 0u;
+                        for (int cc = 0; cc < 8; ++cc)
+                            *reinterpret_cast<uint4*>(tile + cc * 128) =
+                                make_uint4(w[4 * cc], w[4 * cc + 1], w[4 * cc + 2], w[4 * cc + 3]);
+                        fence_proxy_async_smem();
                     }
-                    uint8_t* tile = smem + L.a0 + t * kATile;
-#pragma unroll
-                    for (int cc = 0; cc < 8; ++cc)
-                        *reinterpret_cast<uint4*>(tile + a_offset(j, cc)) =
-                            make_uint4(w[4 * cc], w[4 * cc + 1], w[4 * cc + 2], w[4 * cc + 3]);
-                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(B.a_full(ar.slot));
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(B.a_full(t));
+                if (lane == 0) mbar_arrive(B.raw_empty(rs.slot));
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(B.raw_empty(s));
         }
     }
 
@@ -484,10 +571,14 @@ cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_
                                 static_cast<cuuint64_t>(p.batch)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.channels) * sizeof(T),
                                    static_cast<cuuint64_t>(p.channels) * sizeof(T) * p.length};
-    const cuuint32_t box[3] = {64, kKc, 1};
+    const Layout L = make_layout(cpad, p.length);
+    const cuuint32_t box[3] = {L.vw, kKc, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapSwizzle vswz = L.vw == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                    : L.vw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                 : CU_TENSOR_MAP_SWIZZLE_128B;
     if (encode(&map, dt, 3, const_cast<void*>(p.value), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, vswz,
                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
         CUDA_SUCCESS)
         return cudaErrorNotSupported;
@@ -510,7 +601,7 @@ cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_
         const cuuint64_t adims[2] = {static_cast<cuuint64_t>(p.length + (start - base)),
                                      static_cast<cuuint64_t>(class_rows)};
         const cuuint64_t astrides[1] = {static_cast<cuuint64_t>(p.length) * 8 * sizeof(T)};
-        const cuuint32_t abox[2] = {make_layout(cpad).raw_row / 2, 16};
+        const cuuint32_t abox[2] = {L.raw_row / 2, 16};
         const cuuint32_t aestr[2] = {1, 1};
         if (encode(&amaps.m[r], dt, 2,
                    const_cast<T*>(static_cast<const T*>(p.attention)) + base, adims, astrides,
@@ -519,7 +610,6 @@ cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_
             CUDA_SUCCESS)
             return cudaErrorNotSupported;
     }
-    const Layout L = make_layout(cpad);
     const int64_t tiles =
         static_cast<int64_t>(p.batch) * p.value_heads * ((p.length + kM - 1) / kM);
     const int sms = sm_count();
@@ -541,11 +631,13 @@ cudaError_t launch_zipformer_value_tc(const ZipformerValueProblem& p, cudaStream
     // Rows shorter than one 64-key chunk use the SIMT kernel.
     if (p.length < kKc) return cudaErrorNotSupported;
     // Accumulator columns: the widest head span from its first channel rounded down to 8
-    // (the offset repeats with period 8 in the head index), rounded up to 64.
+    // (the offset repeats with period 8 in the head index), rounded up to the V atom width
+    // (16, 32 or 64 channels).
     const int hd = p.channels / p.value_heads;
     int span = 0;
     for (int h = 0; h < p.value_heads && h < 8; ++h) span = max(span, ((h * hd) & 7) + hd);
-    const int cpad = (span + 63) / 64 * 64;
+    const int vw = span <= 16 ? 16 : span <= 32 ? 32 : 64;
+    const int cpad = (span + vw - 1) / vw * vw;
     if (cpad > kMaxCpad) return cudaErrorNotSupported;
     if (static_cast<int64_t>(p.batch) * p.value_heads * ((p.length + kM - 1) / kM) > (1ll << 30))
         return cudaErrorNotSupported;
