@@ -52,7 +52,8 @@ using namespace sm100;
 
 constexpr int kM = 128;        // query rows per tile
 constexpr int kKc = 64;        // keys per chunk (one 128-byte swizzle atom of A)
-constexpr int kThreads = 352;  // 11 warps
+constexpr int kThreads = 480;  // 15 warps
+constexpr int kRepackWarps = 8;
 constexpr int kMaxCpad = 512;  // TMEM columns
 // Raw staging for a super-chunk of S 64-key chunks: per row a TMA box row of 64*S + 8
 // elements (the class offset is at most 7), 16 rows per residue class, 8 classes.
@@ -96,7 +97,8 @@ __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
 // rows of `seq` keys. A V atom is 64 keys x vw channels (vw = cpad up to 64): rows of
 // 2*vw bytes, swizzled over 2*vw bytes (SWIZZLE_32B, 64B or 128B). Narrow V tiles
 // (cpad <= 128) get 3-chunk super-chunks in a 3-deep raw ring, wide ones single chunks in
-// a 4-deep raw ring; two A tiles. When a V stage per chunk of the whole row fits (at most
+// a 4-deep raw ring. Three A tiles keep the repack and the MMAs from waiting on each
+// other; two when space is short. When a V stage per chunk of the whole row fits (at most
 // kMaxVRes chunks), V is resident: each chunk's stage is loaded once per run of tiles of
 // one (utterance, head) and serves all its query blocks. Otherwise up to kMaxVStages V
 // stages stream; while fewer than 2 fit, the raw ring gives up stages.
@@ -110,13 +112,22 @@ __host__ __device__ constexpr Layout make_layout(int cpad, int seq) {
     l.raw_row = raw_row_bytes(static_cast<int>(l.sup));
     l.raw_stage = raw_stage_bytes(static_cast<int>(l.sup));
     l.raw_stages = narrow ? 3u : 4u;
-    l.a_tiles = 2;
     const uint32_t nchunks = static_cast<uint32_t>((seq + kKc - 1) / kKc);
-    uint32_t fixed = l.raw_stages * l.raw_stage + l.a_tiles * kATile + 1024 + kBarBytes;
-    if (nchunks <= kMaxVRes && fixed + nchunks * l.vstage <= kSmemLimit) {
-        l.vres = 1;
-        l.v_stages = nchunks;
-    } else {
+    for (l.a_tiles = 3; l.a_tiles >= 2 && l.vres == 0; --l.a_tiles) {
+        const uint32_t fixed = l.raw_stages * l.raw_stage + l.a_tiles * kATile + 1024 + kBarBytes;
+        if (nchunks <= kMaxVRes && fixed + nchunks * l.vstage <= kSmemLimit) {
+            l.vres = 1;
+            l.v_stages = nchunks;
+            break;
+        }
+    }
+    if (l.vres == 0) {
+        l.a_tiles = 3;
+        uint32_t fixed = l.raw_stages * l.raw_stage + l.a_tiles * kATile + 1024 + kBarBytes;
+        if (fixed + 3 * l.vstage > kSmemLimit) {
+            l.a_tiles = 2;
+            fixed -= kATile;
+        }
         for (;;) {
             l.v_stages = fixed < kSmemLimit ? (kSmemLimit - fixed) / l.vstage : 0u;
             if (l.v_stages >= 2 || l.raw_stages == 2) break;
@@ -246,10 +257,10 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
     if (tid == 0) {
         for (uint32_t s = 0; s < L.raw_stages; ++s) {
             mbar_init(B.raw_full(s), 1);
-            mbar_init(B.raw_empty(s), 4);
+            mbar_init(B.raw_empty(s), kRepackWarps);
         }
         for (uint32_t t = 0; t < L.a_tiles; ++t) {
-            mbar_init(B.a_full(t), 4);
+            mbar_init(B.a_full(t), kRepackWarps);
             mbar_init(B.a_empty(t), 1);
         }
         for (uint32_t b = 0; b < 2; ++b) {
@@ -358,8 +369,11 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
         uint32_t last_slot = 0, last_phase = 0;
 #pragma unroll 1
         for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
-            if (i == 0 || cur.qb == 0) ++run;
+            const bool run_start = i == 0 || cur.qb == 0;
+            if (run_start) ++run;
             const bool run_end = i + 1 == my_tiles || cur.qb == nqb - 1;
+            // Resident V is waited for once per run: it stays until the run's last tile.
+            const bool wait_v = !L.vres || run_start;
             bool tile_ok = true;
             if (i >= static_cast<int>(L.acc_bufs))
                 tile_ok = warp_wait(B.acc_empty(acc.slot), acc.phase ^ 1u, abort);
@@ -370,7 +384,7 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
                 const uint32_t vph = L.vres ? static_cast<uint32_t>(run & 1) : vr.phase;
                 if (!L.vres) vr.next(L.v_stages);
                 bool ok = tile_ok && warp_wait(B.a_full(ar.slot), ar.phase, abort);
-                ok = ok && warp_wait(B.v_full(vs), vph, abort);
+                if (wait_v) ok = ok && warp_wait(B.v_full(vs), vph, abort);
                 last_slot = ar.slot;
                 last_phase = ar.phase;
                 if (!ok) continue;
@@ -397,7 +411,7 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
         // Teardown: every MMA of this CTA completes before TMEM is released.
         if (!mbar_wait(B.a_empty(last_slot), last_phase) && lane == 0)
             atomicExch(&g_value_tc_error, 1u);
-    } else if (warp >= 7) {
+    } else if (warp >= 7 && warp <= 10) {
         // ---------------- epilogue warps 7..10 ----------------
         const int qtr = warp & 3;
         const int r = qtr * 32 + lane;  // output row = TMEM lane
@@ -444,14 +458,16 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
             if (lane == 0) mbar_arrive(B.acc_empty(acc.slot));
         }
     } else {
-        // ---------------- repack warps 1..4 ----------------
-        // Repack row: thread t = 16 * slot + m handles row j = slot + 8m, so that the 8
-        // lanes of a shared-memory phase read 8 consecutive box rows of one class and
-        // write 8 consecutive core-matrix groups.
-        const int rt = (warp - 1) * 32 + lane;
-        const int slot = rt >> 4, bi = rt & 15;
+        // ---------------- repack warps 1..4 and 11..14 ----------------
+        // Repack thread rt (0..255) moves keys [32 half, 32 half + 32) of row
+        // j = slot + 8 m, with half = rt / 128, slot = (rt / 16) mod 8, m = rt mod 16, so
+        // that the 8 lanes of a shared-memory phase read 8 consecutive box rows of one
+        // class and write 8 consecutive core-matrix groups.
+        const int rt = (warp <= 4 ? warp - 1 : warp - 7) * 32 + lane;
+        const int half = rt >> 7, slot = (rt >> 4) & 7, bi = rt & 15;
         const int j = slot + 8 * bi;
-        const uint32_t a_row = static_cast<uint32_t>(j >> 3) * kSbo + static_cast<uint32_t>(j & 7) * 16u;
+        const uint32_t a_row = static_cast<uint32_t>(j >> 3) * kSbo + static_cast<uint32_t>(j & 7) * 16u +
+                               static_cast<uint32_t>(half) * 512u;
         TileCursor cur;
         cur.init(t_begin, value_heads, nqb);
         Ring rs, ar;
@@ -470,20 +486,20 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
 #pragma unroll 1
             for (int sc = 0; sc < nsup; ++sc, rs.next(L.raw_stages)) {
                 const bool raw_ok = warp_wait(B.raw_full(rs.slot), rs.phase, abort);
-                const uint8_t* raw_row =
-                    smem + L.raw0 + rs.slot * L.raw_stage + (slot * 16 + bi) * L.raw_row;
+                const uint8_t* raw_row = smem + L.raw0 + rs.slot * L.raw_stage +
+                                         (slot * 16 + bi) * L.raw_row + half * 64;
 #pragma unroll 1
                 for (int sub = 0; sub < sup && c < nchunks; ++sub, ++c, ++gc, ar.next(L.a_tiles)) {
                     bool ok = raw_ok;
                     if (ok && gc >= static_cast<int>(L.a_tiles))
                         ok = warp_wait(B.a_empty(ar.slot), ar.phase ^ 1u, abort);
                     if (ok) {
-                        const int nk = min(kKc, seq - c * kKc);
-                        uint32_t w[36];
+                        const int nk = min(kKc, seq - c * kKc) - 32 * half;  // keys of this half
+                        uint32_t w[20];
                         if (q < seq) {
                             const uint4* src = reinterpret_cast<const uint4*>(raw_row + sub * 128);
 #pragma unroll
-                            for (int x = 0; x < 9; ++x) {
+                            for (int x = 0; x < 5; ++x) {
                                 const uint4 v = src[x];
                                 w[4 * x] = v.x;
                                 w[4 * x + 1] = v.y;
@@ -491,14 +507,14 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
                                 w[4 * x + 3] = v.w;
                             }
 #pragma unroll
-                            for (int x = 0; x < 34; ++x) w[x] = (sw & 2u) ? w[x + 2] : w[x];
+                            for (int x = 0; x < 18; ++x) w[x] = (sw & 2u) ? w[x + 2] : w[x];
 #pragma unroll
-                            for (int x = 0; x < 33; ++x) w[x] = (sw & 1u) ? w[x + 1] : w[x];
+                            for (int x = 0; x < 17; ++x) w[x] = (sw & 1u) ? w[x + 1] : w[x];
 #pragma unroll
-                            for (int x = 0; x < 32; ++x) w[x] = __funnelshift_r(w[x], w[x + 1], sh);
-                            if (nk < kKc) {
+                            for (int x = 0; x < 16; ++x) w[x] = __funnelshift_r(w[x], w[x + 1], sh);
+                            if (nk < 32) {
 #pragma unroll
-                                for (int x = 0; x < 32; ++x) {
+                                for (int x = 0; x < 16; ++x) {
                                     const int k = 2 * x;
                                     if (k >= nk) w[x] = 0u;
                                     else if (k + 1 >= nk) w[x] &= 0xFFFFu;
@@ -506,11 +522,11 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
                             }
                         } else {
 #pragma unroll
-                            for (int x = 0; x < 32; ++x) w[x] = 0u;
+                            for (int x = 0; x < 16; ++x) w[x] = 0u;
                         }
                         uint8_t* tile = smem + L.a0 + ar.slot * kATile + a_row;
 #pragma unroll
-                        for (int cc = 0; cc < 8; ++cc)
+                        for (int cc = 0; cc < 4; ++cc)
                             *reinterpret_cast<uint4*>(tile + cc * 128) =
                                 make_uint4(w[4 * cc], w[4 * cc + 1], w[4 * cc + 2], w[4 * cc + 3]);
                         fence_proxy_async_smem();
