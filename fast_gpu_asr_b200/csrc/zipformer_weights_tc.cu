@@ -245,12 +245,16 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
 
     uint32_t ucount = 0;    // score-buffer uses so far (both roles count identically)
     uint32_t kq_phase = 0;  // control warp: Q/K loads so far
+    // Pair tickets are drawn one pair ahead, so the atomic's round trip overlaps the work.
+    if (tid == 0) next_pair[0] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
 #pragma unroll 1
     for (int iter = 0;; ++iter) {
-        if (tid == 0) next_pair[iter & 1] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
         named_barrier(1, kThreads);
         const int pair = next_pair[iter & 1];
         if (pair >= num_pairs) break;
+        // Every thread read slot (iter+1)&1 of the previous pair before this barrier.
+        if (tid == 0)
+            next_pair[(iter + 1) & 1] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
         const int n = pair / heads;
         const int h = pair - n * heads;
         const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
@@ -343,10 +347,12 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             float m_fin = -INFINITY, inv = 0.0f;
             if (block_live) {
                 named_barrier(2, kComputeThreads);  // previous block's band/cache readers done
-                // Positional band of this block: entry i is relative row T-1-q0-127+i.
+                // Positional band of this block: entry i is relative row T-1-q0-127+i. Pass 1
+                // reads entries below 127 + 32 * ngroups.
                 const int band_lo = seq - 1 - q0 - (kM - 1);
+                const int band_fill = min(kBandFill, kM + ngroups * kGroup + 4);
 #pragma unroll 1
-                for (int i = tid; i < kBandFill; i += kComputeThreads) {
+                for (int i = tid; i < band_fill; i += kComputeThreads) {
                     const int rel = band_lo + i;
                     uint2 raw = make_uint2(0u, 0u);
                     if (i < seq + kM - 1 && rel >= 0 && rel < 2 * seq - 1)
