@@ -586,50 +586,98 @@ def ours_arm(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def _pipelined(nlayers_total, h2d, compute, d2h):
+    """Run one step of ``nlayers_total`` layer calls as a three-stream pipeline.
+
+    Layer i copies its inputs in on the copy-in stream, runs on the compute stream and
+    copies its outputs back on the copy-out stream, with device buffers double-buffered
+    by i % 2 and CUDA events ordering the reuse: PCIe carries the inputs of layer i+1
+    and the outputs of layer i-1 (full duplex) while layer i computes. Returns the step
+    function, the stream its first operation runs on and the stream its last one runs
+    on."""
+    import torch
+
+    s_in, s_c, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    h2d_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    d2h_done = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
+
+    def step():
+        for i in range(nlayers_total):
+            b = i % 2
+            if used[b]:
+                s_in.wait_event(comp_done[b])   # inputs of buffer b were read
+            with torch.cuda.stream(s_in):
+                h2d(i, b, s_in)
+                h2d_done[b].record(s_in)
+            s_c.wait_event(h2d_done[b])
+            if used[b]:
+                s_c.wait_event(d2h_done[b])     # outputs of buffer b were copied out
+            with torch.cuda.stream(s_c):
+                compute(i, b, s_c)
+                comp_done[b].record(s_c)
+            s_out.wait_event(comp_done[b])
+            with torch.cuda.stream(s_out):
+                d2h(i, b, s_out)
+                d2h_done[b].record(s_out)
+            used[b] = True
+
+    return step, s_in, s_out
+
+
+def _time_pipeline(step, s_first, s_last, n, world):
+    import torch
+
+    step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record(s_first)
+    for _ in range(n):
+        step()
+    # The last copy-out depends on every earlier operation of the step.
+    end.record(s_last)
+    torch.cuda.synchronize()
+    return allreduce_max(start.elapsed_time(end), world)
+
+
 def e2e_parakeet(args, layers, audio, world):
-    """Same metric through the public API with pinned host inputs and outputs."""
+    """Same metric through the public API with pinned host inputs and outputs, copies
+    overlapped with compute across layers (three-stream pipeline)."""
     import torch
 
     from fast_gpu_asr_b200.attention import parakeet_relative_attention
 
-    stream = torch.cuda.Stream()
-    host_in = []
-    for L in layers[:2]:
-        host_in.append({k: getattr(L, k).cpu().pin_memory() for k in
-                        ("qkv", "position", "content_bias", "position_bias", "valid_lengths")})
-    dev = {k: torch.empty_like(getattr(layers[0], k)) for k in host_in[0]}
-    out = torch.empty((args.batch, 375, 1024), dtype=torch.float16, device="cuda")
-    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host_in[0].values()) * len(layers)
-    d2h = out.numel() * out.element_size() * len(layers)
+    names = ("qkv", "position", "content_bias", "position_bias", "valid_lengths")
+    host_in = [{k: getattr(L, k).cpu().pin_memory() for k in names} for L in layers[:2]]
+    dev = [{k: torch.empty_like(getattr(layers[0], k)) for k in names} for _ in range(2)]
+    outs = [torch.empty((args.batch, 375, 1024), dtype=torch.float16, device="cuda")
+            for _ in range(2)]
+    host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    h2d_bytes = sum(t.numel() * t.element_size() for t in host_in[0].values()) * len(layers)
+    d2h_bytes = outs[0].numel() * outs[0].element_size() * len(layers)
 
-    def step():
-        for i in range(len(layers)):
-            src = host_in[i % 2]
-            for k, t in src.items():
-                dev[k].copy_(t, non_blocking=True)
-            parakeet_relative_attention(dev["qkv"], dev["position"], dev["content_bias"],
-                                        dev["position_bias"], dev["valid_lengths"],
-                                        layers[0].scale, out=out, stream=stream)
-            host_out.copy_(out, non_blocking=True)
+    def h2d(i, b, s):
+        for k, t in host_in[i % 2].items():
+            dev[b][k].copy_(t, non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        step()
-    torch.cuda.synchronize()
+    def compute(i, b, s):
+        d = dev[b]
+        parakeet_relative_attention(d["qkv"], d["position"], d["content_bias"],
+                                    d["position_bias"], d["valid_lengths"], layers[0].scale,
+                                    out=outs[b], stream=s)
+
+    def d2h(i, b, s):
+        host_out[b].copy_(outs[b], non_blocking=True)
+
+    step, s_first, s_last = _pipelined(len(layers), h2d, compute, d2h)
     n = max(1, args.e2e_steps)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        for _ in range(n):
-            step()
-        end.record(stream)
-    torch.cuda.synchronize()
-    ms = allreduce_max(start.elapsed_time(end), world)
+    ms = _time_pipeline(step, s_first, s_last, n, world)
     return {"value": audio * n * world / (ms / 1000.0), "unit": UNIT,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n,
-            "ms_per_step": ms / n}
+            "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes, "steps": n,
+            "ms_per_step": ms / n, "overlap": "copy-in, compute and copy-out streams"}
 
 
 def e2e_zipformer(args, stacks, audio, world):
@@ -638,59 +686,53 @@ def e2e_zipformer(args, stacks, audio, world):
     Per layer the step copies in the projection, positions, mask and the three value
     inputs, runs the weights call and the three attention-value calls, and copies the
     three attention outputs back. The NHTT weights stay on the device, as between two
-    plugins of an engine.
+    plugins of an engine. Copies overlap compute across layers (three-stream pipeline).
     """
     import torch
 
     from fast_gpu_asr_b200.attention import zipformer_attention_value, zipformer_relative_attention
 
-    stream = torch.cuda.Stream()
     names = ("projection", "position", "mask", "value_a", "value_b", "nonlin_value")
-    plan = []
-    h2d = d2h = 0
+    plan = []  # one entry per layer call: (heads, weights, host, dev[2], outs[2], host_outs[2])
+    h2d_bytes = d2h_bytes = 0
     for heads, weights, layers, (out_self, out_nl) in stacks:
         L0 = layers[0]
         host = {k: getattr(L0, k).cpu().pin_memory() for k in names}
-        dev = {k: torch.empty_like(getattr(L0, k)) for k in names}
-        outs = [torch.empty_like(out_self), torch.empty_like(out_self), torch.empty_like(out_nl)]
-        host_outs = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
-        plan.append((heads, weights, len(layers), host, dev, outs, host_outs))
-        h2d += sum(t.numel() * t.element_size() for t in host.values()) * len(layers)
-        d2h += sum(o.numel() * o.element_size() for o in outs) * len(layers)
+        dev = [{k: torch.empty_like(getattr(L0, k)) for k in names} for _ in range(2)]
+        outs = [[torch.empty_like(out_self), torch.empty_like(out_self),
+                 torch.empty_like(out_nl)] for _ in range(2)]
+        host_outs = [[torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs[0]]
+                     for _ in range(2)]
+        for _ in range(len(layers)):
+            plan.append((heads, weights, host, dev, outs, host_outs))
+        h2d_bytes += sum(t.numel() * t.element_size() for t in host.values()) * len(layers)
+        d2h_bytes += sum(o.numel() * o.element_size() for o in outs[0]) * len(layers)
 
-    def step():
-        for heads, weights, nlayers, host, dev, outs, host_outs in plan:
-            for _ in range(nlayers):
-                for k in names:
-                    dev[k].copy_(host[k], non_blocking=True)
-                zipformer_relative_attention(dev["projection"], dev["position"], dev["mask"],
-                                             out=weights, stream=stream)
-                zipformer_attention_value(weights, dev["value_a"], heads, out=outs[0],
-                                          stream=stream)
-                zipformer_attention_value(weights, dev["value_b"], heads, out=outs[1],
-                                          stream=stream)
-                zipformer_attention_value(weights, dev["nonlin_value"], 1, out=outs[2],
-                                          stream=stream)
-                for o, ho in zip(outs, host_outs):
-                    ho.copy_(o, non_blocking=True)
+    def h2d(i, b, s):
+        heads, weights, host, dev, outs, host_outs = plan[i]
+        for k in names:
+            dev[b][k].copy_(host[k], non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        step()
-    torch.cuda.synchronize()
+    def compute(i, b, s):
+        heads, weights, host, dev, outs, host_outs = plan[i]
+        d, o = dev[b], outs[b]
+        zipformer_relative_attention(d["projection"], d["position"], d["mask"], out=weights,
+                                     stream=s)
+        zipformer_attention_value(weights, d["value_a"], heads, out=o[0], stream=s)
+        zipformer_attention_value(weights, d["value_b"], heads, out=o[1], stream=s)
+        zipformer_attention_value(weights, d["nonlin_value"], 1, out=o[2], stream=s)
+
+    def d2h(i, b, s):
+        heads, weights, host, dev, outs, host_outs = plan[i]
+        for o, ho in zip(outs[b], host_outs[b]):
+            ho.copy_(o, non_blocking=True)
+
+    step, s_first, s_last = _pipelined(len(plan), h2d, compute, d2h)
     n = max(1, args.e2e_steps)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        for _ in range(n):
-            step()
-        end.record(stream)
-    torch.cuda.synchronize()
-    ms = allreduce_max(start.elapsed_time(end), world)
+    ms = _time_pipeline(step, s_first, s_last, n, world)
     return {"value": audio * n * world / (ms / 1000.0), "unit": UNIT,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n,
-            "ms_per_step": ms / n}
+            "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes, "steps": n,
+            "ms_per_step": ms / n, "overlap": "copy-in, compute and copy-out streams"}
 
 
 def main():
