@@ -260,6 +260,81 @@ def test_value_full_size_stack1_linearity():
                                        atol=1e-2)
 
 
+# Long rows reach every shared-memory plan of the attention-value kernel: V resident per
+# (utterance, head) with three or two A tiles (T <= 1024), V streamed per chunk (T > 1024),
+# 16-, 32- and 64-channel V atoms, and single-chunk boxes for wide value tiles.
+LONG_VALUE_LAYERS = (("self", 4, 4, 48), ("two_heads_32", 2, 2, 64), ("nonlinear_wide", 4, 1, 288))
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("layer", LONG_VALUE_LAYERS, ids=[c[0] for c in LONG_VALUE_LAYERS])
+@pytest.mark.parametrize("length", [700, 1000, 1025, 1100])
+def test_value_long_rows_cover_every_layout(dtype, layer, length):
+    name, ah, vh, ch = layer
+    a, v = cases.value_inputs(1, length, ah, ch, seed=4000 + length)
+    got = value_on_gpu(a, v, vh, dtype)
+    expected = oracle_value(a, v, vh, dtype)
+    tol = cases.VALUE_TOL[dtype]
+    np.testing.assert_allclose(got, expected, rtol=tol, atol=tol)
+
+
+def test_value_guard_bands_graph_replay_and_streams():
+    """Output inside a larger buffer (guard bands untouched), CUDA-graph replay, and two
+    problems on two streams at once (each CTA takes its own contiguous tile range)."""
+    a1, v1 = cases.value_inputs(2, 300, 4, 48, seed=51)
+    a2, v2 = cases.value_inputs(3, 200, 4, 288, seed=52)
+    dt = torch.bfloat16
+    at1, vt1 = torch.from_numpy(a1).to("cuda", dt), torch.from_numpy(v1).to("cuda", dt)
+    at2, vt2 = torch.from_numpy(a2).to("cuda", dt), torch.from_numpy(v2).to("cuda", dt)
+    n1 = vt1.numel()
+    store = torch.full((n1 + 512,), 7, dtype=dt, device="cuda")
+    out1 = store[256 : 256 + n1].view(vt1.shape)
+    out2 = torch.full_like(vt2, float("nan"))
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    with torch.cuda.stream(s1):
+        zipformer_attention_value(at1, vt1, 4, out=out1, stream=s1)
+    with torch.cuda.stream(s2):
+        zipformer_attention_value(at2, vt2, 1, out=out2, stream=s2)
+    torch.cuda.synchronize()
+    assert (store[:256] == 7).all() and (store[256 + n1 :] == 7).all()
+    first1, first2 = out1.float().cpu().numpy(), out2.float().cpu().numpy()
+    np.testing.assert_allclose(first1, oracle_value(a1, v1, 4, "bfloat16"), rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(first2, oracle_value(a2, v2, 1, "bfloat16"), rtol=1e-2, atol=1e-2)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s1):
+        zipformer_attention_value(at1, vt1, 4, out=out1, stream=s1)
+    for _ in range(2):
+        out1.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out1.float().cpu().numpy(), first1)
+    assert (store[:256] == 7).all() and (store[256 + n1 :] == 7).all()
+
+
+def test_weights_on_concurrent_streams():
+    """Two weights problems in flight on two streams (each launch draws its own pair
+    scheduling slot) match their one-at-a-time results."""
+    xs = [cases.zipformer_inputs(3, 200), cases.zipformer_inputs(2, 375)]
+    serial = [weights_on_gpu(x, "bfloat16") for x in xs]
+    dt = torch.bfloat16
+    args, outs = [], []
+    for x in xs:
+        proj = torch.from_numpy(x["projection"]).to("cuda", dt)
+        pos = torch.from_numpy(x["position"]).to("cuda", dt)
+        mask = torch.from_numpy(np.asarray(x["mask"], bool)).cuda()
+        n, t = proj.shape[:2]
+        args.append((proj, pos, mask))
+        outs.append(torch.full((n, pos.shape[2], t, t), float("nan"), dtype=dt, device="cuda"))
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for _ in range(3):
+        for (proj, pos, mask), out, s in zip(args, outs, streams):
+            with torch.cuda.stream(s):
+                zipformer_relative_attention(proj, pos, mask, out=out, stream=s)
+    torch.cuda.synchronize()
+    for out, ref in zip(outs, serial):
+        np.testing.assert_array_equal(out.float().cpu().numpy(), ref)
+
+
 def test_variant_reported():
     a, v = cases.value_inputs(1, 33, 4, 48, seed=1)
     value_on_gpu(a, v, 4, "bfloat16")
