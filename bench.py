@@ -1,12 +1,15 @@
 """Encoder-attention benchmark: audio-seconds per second through the attention plugins.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload parakeet|zipformer]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload parakeet|parakeet_long|zipformer|ragged]
     python bench.py --impl reference ...   # the reference math on the host cores
 
 A *step* is one encoder forward's worth of attention calls over one batch:
 * ``parakeet`` (default): 24 Conformer layers of
   ``parakeet_relative_attention`` on 256 utterances x 375 frames, fp16, 8 x 128 heads,
   each layer with its own inputs (590 MB of QKV per layer, far above the 126 MB L2).
+* ``parakeet_long`` (config 4, long-form): the same on 16 utterances x 3000 frames with
+  valid lengths U[1500, 3000] (295 MB of QKV per layer).
 * ``zipformer``: every layer of the six Zipformer stacks
   (2/2/4/5/4/2 layers at T = 750/375/188/94/188/375), each layer one
   ``zipformer_relative_attention`` call plus three ``zipformer_attention_value`` calls,
@@ -45,13 +48,27 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("parakeet", "zipformer", "ragged"), default="parakeet")
-    p.add_argument("--batch", type=int, default=256)
+    p.add_argument("--workload", choices=("parakeet", "parakeet_long", "zipformer", "ragged"),
+                   default="parakeet")
+    p.add_argument("--batch", type=int, default=None,
+                   help="utterances per GPU (default 256; 16 for parakeet_long)")
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    return p.parse_args()
+    args = p.parse_args()
+    if args.batch is None:
+        args.batch = 16 if args.workload == "parakeet_long" else 256
+    return args
+
+
+def parakeet_shape(args):
+    """(frames, shortest valid length) of the Parakeet workload: config 2 or config 4."""
+    return (3000, 1500) if args.workload == "parakeet_long" else (375, 60)
+
+
+def is_parakeet(args) -> bool:
+    return args.workload in ("parakeet", "parakeet_long")
 
 
 def load_peaks() -> dict:
@@ -176,16 +193,17 @@ def build_parakeet(args, rank):
 
     from fast_gpu_asr_b200 import workloads as wl
 
+    frames, low = parakeet_shape(args)
     layers = []
     for i in range(wl.PARAKEET_LAYERS):
-        lens = wl.parakeet_lengths(args.batch, 375, 60, seed=1000 * rank + 7)
-        layers.append(wl.make_parakeet_layer(args.batch, 375, 8, 128, torch.float16, "cuda",
+        lens = wl.parakeet_lengths(args.batch, frames, low, seed=1000 * rank + 7)
+        layers.append(wl.make_parakeet_layer(args.batch, frames, 8, 128, torch.float16, "cuda",
                                              seed=1000 * rank + i, lengths=lens))
     torch.cuda.synchronize()
     audio = wl.parakeet_audio_seconds(layers[0].valid_lengths)
-    flops = wl.parakeet_flops(layers[0].valid_lengths, 375, 8, 128)
-    nbytes = wl.parakeet_bytes(args.batch, 375, 8, 128, 2)
-    outs = [torch.empty((args.batch, 375, 1024), dtype=torch.float16, device="cuda")
+    flops = wl.parakeet_flops(layers[0].valid_lengths, frames, 8, 128)
+    nbytes = wl.parakeet_bytes(args.batch, frames, 8, 128, 2)
+    outs = [torch.empty((args.batch, frames, 1024), dtype=torch.float16, device="cuda")
             for _ in range(2)]
     return layers, outs, audio, flops, nbytes
 
@@ -269,16 +287,17 @@ def run_zipformer_step(stacks, stream, events=None):
 
 
 # ---- CPU legs (oracle port of the reference math) -----------------------------------------
-def cpu_parakeet(seconds: float):
-    """Time the oracle (reference math restated on torch CPU) on config-2 utterances."""
+def cpu_parakeet(seconds: float, frames: int = 375, low: int = 60, per_call: int = 4):
+    """Time the oracle (reference math restated on torch CPU) on config-2 (or, with
+    frames=3000, config-4) utterances."""
     import torch
 
     from fast_gpu_asr_b200 import workloads as wl
     from oracle import parakeet_relative_attention as oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
-    per_call = 4
-    layer = wl.make_parakeet_layer(per_call, 375, 8, 128, torch.float16, "cpu", seed=11)
+    layer = wl.make_parakeet_layer(per_call, frames, 8, 128, torch.float16, "cpu", seed=11,
+                                   length_low=low)
     args = dict(qkv=layer.qkv.float().numpy(), position=layer.position.float().numpy(),
                 content_bias=layer.content_bias.float().numpy(),
                 position_bias=layer.position_bias.float().numpy(),
@@ -293,7 +312,7 @@ def cpu_parakeet(seconds: float):
         if elapsed >= seconds:
             break
     value = audio * calls / (elapsed * wl.PARAKEET_LAYERS)
-    sample = (f"{calls} calls x {per_call} utterances x 375 frames (8x128 heads, fp16 "
+    sample = (f"{calls} calls x {per_call} utterances x {frames} frames (8x128 heads, fp16 "
               f"rounding) = {calls} of the 24 per-forward layer calls on a {per_call}-utterance "
               f"slice; scaled to a 24-layer forward")
     return value, torch.get_num_threads(), sample
@@ -335,11 +354,18 @@ def cpu_zipformer(seconds: float):
     return value, torch.get_num_threads(), sample
 
 
+def cpu_leg(args):
+    """The CPU timing function of the workload (seconds -> value, cores, sample)."""
+    if args.workload == "parakeet_long":
+        return lambda seconds: cpu_parakeet(seconds, 3000, 1500, 1)
+    return cpu_parakeet if args.workload == "parakeet" else cpu_zipformer
+
+
 def reference_arm(args, world, rank):
     """`--impl reference`: the reference math (oracle port) on the host cores, rank 0 only."""
     if rank != 0:
         return
-    fn = cpu_parakeet if args.workload == "parakeet" else cpu_zipformer
+    fn = cpu_leg(args)
     per_step = []
     for _ in range(args.warmup):
         fn(min(2.0, args.cpu_seconds))
@@ -361,6 +387,11 @@ def reference_arm(args, world, rank):
 
 
 def workload_config(args) -> dict:
+    if args.workload == "parakeet_long":
+        return {"workload": "parakeet_relative_attention (config 4, long-form)",
+                "batch": args.batch, "frames": 3000, "heads": 8, "head_dim": 128, "layers": 24,
+                "lengths": "U[1500,3000]", "dtype": "f16", "parallelism": f"dp{args.gpus}",
+                "l2": "inputs exceed L2 (295 MB QKV per layer, 24 distinct layers)"}
     if args.workload == "parakeet":
         return {"workload": "parakeet_relative_attention (config 2)", "batch": args.batch,
                 "frames": 375, "heads": 8, "head_dim": 128, "layers": 24,
@@ -472,7 +503,7 @@ def ours_arm(args, world, rank, local):
     if bus is not None:
         bus_id = f"{getattr(dev_props, 'pci_domain_id', 0):08x}:{bus:02x}:{getattr(dev_props, 'pci_device_id', 0):02x}.0"
 
-    if args.workload == "parakeet":
+    if is_parakeet(args):
         layers, outs, audio, flops, nbytes = build_parakeet(args, rank)
         launch_kinds = [("parakeet_relative_attention", nbytes)] * len(layers)
 
@@ -535,7 +566,7 @@ def ours_arm(args, world, rank, local):
     avg_launch_ms = dk["ms"] / dk["launches"]
     avg_bytes = dk["bytes"] / dk["launches"]
 
-    if args.workload == "parakeet":
+    if is_parakeet(args):
         achieved = flops / (avg_launch_ms / 1000.0) / 1e12
         roofline = {"bound": "tensor", "kernel": dominant, "achieved": achieved,
                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -564,15 +595,14 @@ def ours_arm(args, world, rank, local):
 
     e2e = None
     if not args.no_e2e:
-        if args.workload == "parakeet":
+        if is_parakeet(args):
             e2e = e2e_parakeet(args, layers, audio, world)
         else:
             e2e = e2e_zipformer(args, stacks, audio, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        fn = cpu_parakeet if args.workload == "parakeet" else cpu_zipformer
-        v, cores, sample = fn(args.cpu_seconds)
+        v, cores, sample = cpu_leg(args)(args.cpu_seconds)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
@@ -653,8 +683,8 @@ def e2e_parakeet(args, layers, audio, world):
     names = ("qkv", "position", "content_bias", "position_bias", "valid_lengths")
     host_in = [{k: getattr(L, k).cpu().pin_memory() for k in names} for L in layers[:2]]
     dev = [{k: torch.empty_like(getattr(layers[0], k)) for k in names} for _ in range(2)]
-    outs = [torch.empty((args.batch, 375, 1024), dtype=torch.float16, device="cuda")
-            for _ in range(2)]
+    outs = [torch.empty((args.batch, layers[0].qkv.shape[1], 1024), dtype=torch.float16,
+                        device="cuda") for _ in range(2)]
     host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
     h2d_bytes = sum(t.numel() * t.element_size() for t in host_in[0].values()) * len(layers)
     d2h_bytes = outs[0].numel() * outs[0].element_size() * len(layers)
