@@ -180,6 +180,19 @@ def allreduce_max(x: float, world: int) -> float:
     return float(t.item())
 
 
+def allgather_floats(x: float, world: int) -> list:
+    """Every rank's value of ``x``, in rank order (one collective, all ranks call it)."""
+    if world == 1:
+        return [x]
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
 def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
@@ -470,6 +483,7 @@ def ragged_arm(args, world, rank, local):
         del players, stacks
     barrier(world)
     max_ms = allreduce_max(kernel_ms, world)
+    rank_ms = allgather_floats(kernel_ms, world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     gathered = gather_to_rank0(outputs, shapes, world, rank, "cuda", torch.float16)
@@ -483,7 +497,7 @@ def ragged_arm(args, world, rank, local):
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f16+bf16", "data": "synthetic", "config": workload_config(args),
                 "batches": len(plan), "batches_per_rank": len(mine),
-                "gather_wall_s": gather_s, "gpu_launches": launches,
+                "rank_busy_ms": rank_ms, "gather_wall_s": gather_s, "gpu_launches": launches,
                 "variant": _lib.last_kernel_variant()}
         print(json.dumps(line), flush=True)
 
