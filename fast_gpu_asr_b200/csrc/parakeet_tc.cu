@@ -17,9 +17,10 @@
 // halves 0 and 1 together with S_c(0), half j+2 together with S_c(j+1). The score MMAs
 // then do exactly the algorithmic work (no band recomputation).
 //
-// Skew. A warp loads the 64-column window its 32 rows span (two 32-column pieces, each
-// inside one half) and every thread shifts its own row into place with a 5-stage
-// predicated barrel shift.
+// Skew. A warp loads the 96-column band window its 32 rows and 64 keys span (three
+// 32-column pieces, each inside one half) together with its S_c columns, releases S at
+// once, and every thread then shifts its own row into place with a 5-stage predicated
+// barrel shift while the MMA warp computes the next tile's scores.
 //
 // CTA organisation (persistent: one CTA per SM walks the work items):
 //   warps 0-7  softmax. Warp w owns TMEM lanes 32*(w%4).. (rows) and key half w/4 (64
@@ -38,9 +39,9 @@
 // in fp32 (:503-508); only keys below the valid length contribute; valid_length <= 0
 // gives zero rows (:478-486); every query row < T is produced (:472-476). Scores stay
 // in fp32 between the GEMMs (the reference stores them in the I/O dtype). log2(e) is
-// folded into the scale, so this kernel serves scale <= 1 (every real model:
-// 1/sqrt(D)); larger scales run on the SIMT kernel, which subtracts the row max
-// before converting to base 2 exactly like the reference.
+// folded into the scale and the row max is taken before scaling, so this kernel serves
+// 0 < scale <= 1 (every real model: 1/sqrt(D)); other scales run on the SIMT kernel,
+// which subtracts the row max before converting to base 2 exactly like the reference.
 //
 // Data movement: Q, K and V tiles arrive by TMA from the fused [N, T, 3C] projection
 // through a 3-D tensor map (rows past T of an utterance read as zero), positional
@@ -81,7 +82,9 @@ constexpr uint32_t kSmemP = kSmemB0 + 2 * kTile;
 constexpr uint32_t kSmemXchg = kSmemP + kTile;  // [2 halves][128 rows] fp32
 constexpr uint32_t kLenCache = 256;             // valid lengths of utterances 0..255
 constexpr uint32_t kSmemLen = kSmemXchg + 2 * kM * 4;
-constexpr uint32_t kSmemBar = kSmemLen + kLenCache * 4;
+constexpr uint32_t kSmemBias = kSmemLen + kLenCache * 4;  // [u | v] of the item's head
+constexpr uint32_t kBiasBytes = 2 * kD * 2;
+constexpr uint32_t kSmemBar = kSmemBias + kBiasBytes;
 constexpr uint32_t kNumBars = 17;
 constexpr uint32_t kSmemBytes = kSmemBar + kNumBars * 8 + 16;
 
@@ -97,6 +100,7 @@ enum : uint32_t {
     kBarBEmpty0              // slot s empty: kBarBEmpty0 + s (entries 15 and 16)
 };
 static_assert(kBarBEmpty0 + 2 == kNumBars, "barrier table");
+static_assert(kSmemBias % 16 == 0 && kSmemBytes <= 227 * 1024, "shared-memory map");
 
 __device__ unsigned int g_parakeet_tc_error = 0;
 
@@ -113,14 +117,6 @@ template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, fl
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
 }
-template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t w);
-template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
-    return __half22float2(*reinterpret_cast<__half2*>(&w));
-}
-template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
-    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w));
-}
-
 // 2^x on the MUFU unit (ex2.approx, relative error ~2^-22; -inf -> 0).
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
@@ -132,18 +128,22 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// out[j] = v[j + s] for j < 32, s in [0, 31]: five predicated stages (16, 8, 4, 2, 1).
-__device__ __forceinline__ void barrel_shift(uint32_t (&v)[64], uint32_t s) {
+// out[j] = v[j + s] for j < 64, s in [0, 31]: five predicated stages (16, 8, 4, 2, 1),
+// each touching only the entries the later stages still read. The coarse stages leave
+// entries 71..95 dead; the fine stages finish the shift.
+__device__ __forceinline__ void barrel_shift_coarse(uint32_t (&v)[96], uint32_t s) {
 #pragma unroll
-    for (int j = 0; j < 47; ++j) v[j] = (s & 16u) ? v[j + 16] : v[j];
+    for (int j = 0; j < 79; ++j) v[j] = (s & 16u) ? v[j + 16] : v[j];
 #pragma unroll
-    for (int j = 0; j < 39; ++j) v[j] = (s & 8u) ? v[j + 8] : v[j];
+    for (int j = 0; j < 71; ++j) v[j] = (s & 8u) ? v[j + 8] : v[j];
+}
+__device__ __forceinline__ void barrel_shift_fine(uint32_t (&v)[96], uint32_t s) {
 #pragma unroll
-    for (int j = 0; j < 35; ++j) v[j] = (s & 4u) ? v[j + 4] : v[j];
+    for (int j = 0; j < 67; ++j) v[j] = (s & 4u) ? v[j + 4] : v[j];
 #pragma unroll
-    for (int j = 0; j < 33; ++j) v[j] = (s & 2u) ? v[j + 2] : v[j];
+    for (int j = 0; j < 65; ++j) v[j] = (s & 2u) ? v[j + 2] : v[j];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = (s & 1u) ? v[j + 1] : v[j];
+    for (int j = 0; j < 64; ++j) v[j] = (s & 1u) ? v[j + 1] : v[j];
 }
 
 template <int N> __device__ __forceinline__ float tree_max(const float (&x)[N]) {
@@ -216,67 +216,77 @@ __device__ __forceinline__ uint32_t band_col(uint32_t x, uint32_t slot_lo) {
     return kColBand + slot * 128u + (x & 127u);
 }
 
-// Scaled base-2 logits of this thread's 64 keys of the tile (two 32-key chunks).
+// This thread's row of the tile as it sits in TMEM: the 96 band columns its 64 keys
+// reach (rows of a warp span 32 band columns, so the window is [base, base + 96) with
+// base = 96 - 32 group + 64 half, in three 32-column pieces that each lie inside one ring
+// slot), then S_c of those keys. The coarse shift stages run between the two loads so
+// that fewer values are live at once. Every load completes here, so the caller can
+// release S before the rest of the arithmetic and the next tile's score MMAs overlap
+// the skew and the exponentials.
+__device__ __forceinline__ void load_tile(uint32_t (&sc)[kHalfKeys], uint32_t (&band)[96],
+                                          uint32_t tmem_row, int group, int half,
+                                          uint32_t slot_lo, uint32_t shift) {
+    const uint32_t base = 96u - 32u * group + 64u * half;
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+        tmem_ld32(tmem_row + band_col(base + 32u * p, slot_lo),
+                  *reinterpret_cast<uint32_t(*)[32]>(band + 32 * p));
+    tmem_wait_ld();
+#pragma unroll
+    for (int p = 0; p < 3; ++p) reg_fence(*reinterpret_cast<uint32_t(*)[32]>(band + 32 * p));
+    barrel_shift_coarse(band, shift);
+    tmem_ld64(tmem_row + kColSc + half * 64, sc);
+    tmem_wait_ld();
+    reg_fence(sc);
+}
+
+// Unscaled logits S_c + band of this thread's 64 keys (row lane of its warp reads band
+// column base + key + 31 - lane); keys at or past the valid length are -inf.
 template <bool kMasked>
-__device__ __forceinline__ void load_logits(float (&s)[kHalfKeys], uint32_t tmem_row,
-                                            int group, int half, uint32_t shift,
-                                            uint32_t slot_lo, float scale_log2, int nvalid) {
+__device__ __forceinline__ void form_logits(float (&s)[kHalfKeys],
+                                            const uint32_t (&sc)[kHalfKeys],
+                                            uint32_t (&band)[96], uint32_t shift, int nvalid) {
+    barrel_shift_fine(band, shift);
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-        const int c = 2 * half + cc;  // 32-key chunk of the tile
-        uint32_t sc[32], band[64];
-        const uint32_t base = 96u - 32u * group + 32u * c;  // band window [base, base+64)
-        tmem_ld32(tmem_row + kColSc + c * 32, sc);
-        tmem_ld32(tmem_row + band_col(base, slot_lo), *reinterpret_cast<uint32_t(*)[32]>(band));
-        tmem_ld32(tmem_row + band_col(base + 32, slot_lo),
-                  *reinterpret_cast<uint32_t(*)[32]>(band + 32));
-        tmem_wait_ld();
-        reg_fence(sc);
-        reg_fence(band);
-        barrel_shift(band, shift);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            const float v = (__uint_as_float(sc[e]) + __uint_as_float(band[e])) * scale_log2;
-            s[cc * 32 + e] = (!kMasked || c * 32 + e < nvalid) ? v : -INFINITY;
-        }
+    for (int e = 0; e < kHalfKeys; ++e) {
+        const float v = __uint_as_float(sc[e]) + __uint_as_float(band[e]);
+        s[e] = (!kMasked || e < nvalid) ? v : -INFINITY;
     }
 }
 
-// (Q+u), (Q+v) in fp32, rounded to T (reference .cu:268-281), for this warp's 32 rows
-// and head channels [64*half, 64*half+64). One 8-channel chunk at a time keeps few
-// registers live (this runs while the current tile's logits are held in registers);
-// the bias vectors are L1-resident after the first warp reads them.
+// Two packed T values added with one round-to-nearest packed add. The reference forms
+// the biased queries in fp32 and rounds the sum to T (reference .cu:268-281). For f16
+// (11-bit significand) and bf16 (8-bit) inputs the fp32 sum rounded to T equals the
+// correctly rounded T sum: double rounding through a format of p' >= 2p + 1 significand
+// bits is innocuous for addition (S. A. Figueroa, "When is double rounding innocuous?",
+// SIGNUM Newsletter 30(3), 1995), and fp32 has p' = 24.
+template <typename T> __device__ __forceinline__ uint32_t add2(uint32_t a, uint32_t b);
+template <> __device__ __forceinline__ uint32_t add2<__half>(uint32_t a, uint32_t b) {
+    __half2 r = __hadd2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+template <> __device__ __forceinline__ uint32_t add2<__nv_bfloat16>(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hadd2(*reinterpret_cast<__nv_bfloat162*>(&a),
+                               *reinterpret_cast<__nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Q+u and Q+v rounded to T (see add2) for this thread's row and head channels
+// [64*half, 64*half+64), in place in the Qu tile and into the Qv tile. The item's u and v
+// rows arrive in shared memory with its Q tile.
 template <typename T>
-__device__ __forceinline__ void bias_queries(uint8_t* smem, const T* __restrict__ ub,
-                                             const T* __restrict__ vb, int row, int half) {
-#pragma unroll 1
-    for (int g4 = 0; g4 < 2; ++g4) {
-        uint4 uw4[4], vw4[4];
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-            const int c = half * 8 + g4 * 4 + c4;
-            uw4[c4] = __ldg(reinterpret_cast<const uint4*>(ub + c * 8));
-            vw4[c4] = __ldg(reinterpret_cast<const uint4*>(vb + c * 8));
-        }
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-            const uint32_t off = half * kAtom + sw128_offset(row, g4 * 4 + c4);
-            const uint4 qw = *reinterpret_cast<const uint4*>(smem + kSmemQu + off);
-            const uint32_t qs[4] = {qw.x, qw.y, qw.z, qw.w};
-            const uint32_t us[4] = {uw4[c4].x, uw4[c4].y, uw4[c4].z, uw4[c4].w};
-            const uint32_t vs[4] = {vw4[c4].x, vw4[c4].y, vw4[c4].z, vw4[c4].w};
-            uint32_t a[4], b[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 q = unpack2<T>(qs[e]);
-                const float2 u = unpack2<T>(us[e]);
-                const float2 v = unpack2<T>(vs[e]);
-                a[e] = pack2<T>(q.x + u.x, q.y + u.y);
-                b[e] = pack2<T>(q.x + v.x, q.y + v.y);
-            }
-            *reinterpret_cast<uint4*>(smem + kSmemQu + off) = make_uint4(a[0], a[1], a[2], a[3]);
-            *reinterpret_cast<uint4*>(smem + kSmemQv + off) = make_uint4(b[0], b[1], b[2], b[3]);
-        }
+__device__ __forceinline__ void bias_queries(uint8_t* smem, int row, int half) {
+    const uint4* ub = reinterpret_cast<const uint4*>(smem + kSmemBias) + half * 8;
+    const uint4* vb = reinterpret_cast<const uint4*>(smem + kSmemBias + 2 * kD) + half * 8;
+#pragma unroll 4
+    for (int c = 0; c < 8; ++c) {
+        const uint32_t off = half * kAtom + sw128_offset(row, c);
+        const uint4 q = *reinterpret_cast<const uint4*>(smem + kSmemQu + off);
+        const uint4 u = ub[c], v = vb[c];
+        *reinterpret_cast<uint4*>(smem + kSmemQu + off) = make_uint4(
+            add2<T>(q.x, u.x), add2<T>(q.y, u.y), add2<T>(q.z, u.z), add2<T>(q.w, u.w));
+        *reinterpret_cast<uint4*>(smem + kSmemQv + off) = make_uint4(
+            add2<T>(q.x, v.x), add2<T>(q.y, v.y), add2<T>(q.z, v.z), add2<T>(q.w, v.w));
     }
 }
 
@@ -382,10 +392,13 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 if (it.tiles == 0) continue;
                 prefetch_item(item + gridDim.x);
                 if (q_iter > 0 && !(ok = sync.wait(kBarQEmpty, (q_iter - 1) & 1))) break;
-                mbar_expect_tx(sync.bar(kBarQFull), kTile);
+                mbar_expect_tx(sync.bar(kBarQFull), kTile + kBiasBytes);
                 tma_load_3d(sbase + kSmemQu, &qkv_map, sync.bar(kBarQFull), it.h * kD, it.q0, it.n);
                 tma_load_3d(sbase + kSmemQu + kAtom, &qkv_map, sync.bar(kBarQFull),
                             it.h * kD + 64, it.q0, it.n);
+                bulk_load(sbase + kSmemBias, ubias + it.h * kD, 2 * kD, sync.bar(kBarQFull));
+                bulk_load(sbase + kSmemBias + 2 * kD, vbias + it.h * kD, 2 * kD,
+                          sync.bar(kBarQFull));
                 ++q_iter;
                 // In the order the MMA consumes them: K(0), chunk 0, chunk 1, then
                 // K(j), chunk j+1 for j >= 1.
@@ -568,11 +581,10 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
             }
             return item;
         };
-        auto prepare_queries = [&](int item) -> bool {
-            const Item it = decode_item(item, qtiles, heads, length, lengths);
+        auto prepare_queries = [&]() -> bool {
             if (!sync.wait_warp(kBarQFull, q_iter & 1)) return false;
             ++q_iter;
-            bias_queries<T>(smem, ubias + it.h * kD, vbias + it.h * kD, row, half);
+            bias_queries<T>(smem, row, half);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(sync.bar(kBarQReady));
@@ -580,7 +592,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
         };
 
         int item = next_item(blockIdx.x);
-        if (item < num_items) ok = prepare_queries(item);
+        if (item < num_items) ok = prepare_queries();
         while (ok && item < num_items) {
             const Item it = decode_item(item, qtiles, heads, length, lengths);
             // The candidate's length load is issued now and consumed at the last tile.
@@ -594,22 +606,27 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 if (!(ok = sync.wait_warp(kBarSFull, s_iter & 1))) break;
                 ++s_iter;
                 tc_fence_after();
-                float s[kHalfKeys];
                 const int nvalid = it.valid - k0;  // valid keys in this tile (>= 1)
                 const uint32_t slot_lo = (h_base + j) & 1;
-                if (nvalid >= kN)
-                    load_logits<false>(s, tmem_row, group, half, shift, slot_lo, scale_log2, nvalid);
-                else
-                    load_logits<true>(s, tmem_row, group, half, shift, slot_lo, scale_log2, nvalid);
-                // Scores are in registers: the MMA warp may overwrite S with the next tile.
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(sync.bar(kBarSFree));
+                float s[kHalfKeys];
+                {
+                    uint32_t sc[kHalfKeys], band[96];
+                    load_tile(sc, band, tmem_row, group, half, slot_lo, shift);
+                    // Scores are in registers: the MMA warp may overwrite S with the next tile.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(sync.bar(kBarSFree));
+                    if (nvalid >= kN)
+                        form_logits<false>(s, sc, band, shift, kHalfKeys);
+                    else
+                        form_logits<true>(s, sc, band, shift, nvalid - half * kHalfKeys);
+                }
 
                 const float m_half = tree_max(s);
                 xchg[half * kM + row] = m_half;
                 named_barrier(pair_bar, 64);
-                const float m_tile = fmaxf(m_half, xchg[(1 - half) * kM + row]);
+                // Scaled base-2 tile max: scale_log2 > 0, so scaling commutes with max.
+                const float m_tile = fmaxf(m_half, xchg[(1 - half) * kM + row]) * scale_log2;
                 named_barrier(pair_bar, 64);  // the slot is rewritten next tile
                 // Move the reference max only when it grows by more than 2^8.
                 const bool grow = (m_tile - m_run) > kRescaleThreshold;
@@ -628,8 +645,8 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                     uint32_t w[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float p0 = fast_exp2(s[c * 8 + 2 * e] - m_new);
-                        const float p1 = fast_exp2(s[c * 8 + 2 * e + 1] - m_new);
+                        const float p0 = fast_exp2(fmaf(s[c * 8 + 2 * e], scale_log2, -m_new));
+                        const float p1 = fast_exp2(fmaf(s[c * 8 + 2 * e + 1], scale_log2, -m_new));
                         lsum[e] += p0 + p1;
                         w[e] = pack2<T>(p0, p1);
                     }
@@ -662,7 +679,7 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 // last P.V runs; its first score MMAs then run under this epilogue.
                 if (j + 1 == it.tiles && cand < num_items) {
                     next = cand_len > 0 ? cand : next_item(cand);
-                    if (next < num_items && !(ok = prepare_queries(next))) break;
+                    if (next < num_items && !(ok = prepare_queries())) break;
                 }
             }
             if (!ok) break;
@@ -796,7 +813,8 @@ bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u
 cudaError_t launch_parakeet_tc(const ParakeetProblem& p, cudaStream_t stream) {
     if (p.head_dim != kD || (p.dtype != FGA_HALF && p.dtype != FGA_BF16)) return cudaErrorNotSupported;
     // log2(e) is folded into the scale; keep scaled logits far from the fp32 range limit.
-    if (!(p.scale <= 1.0f)) return cudaErrorNotSupported;
+    // The tile max is taken before scaling, which needs a positive scale.
+    if (!(p.scale > 0.0f && p.scale <= 1.0f)) return cudaErrorNotSupported;
     if (static_cast<int64_t>((p.length + kM - 1) / kM) * p.heads * p.batch > 0x7fffffff)
         return cudaErrorNotSupported;
     if (!aligned16(p.qkv) || !aligned16(p.position) || !aligned16(p.output) ||
