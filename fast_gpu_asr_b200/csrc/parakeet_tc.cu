@@ -45,8 +45,10 @@
 //
 // Data movement: Q, K and V tiles arrive by TMA from the fused [N, T, 3C] projection
 // through a 3-D tensor map (rows past T of an utterance read as zero), positional
-// chunks through a 2-D map over [2T-1, C] (rows outside the table read as zero). All
-// operand tiles use the 128-byte-swizzled canonical UMMA layouts.
+// chunks through a 2-D map over [2T-1, C] (rows outside the table read as zero), the
+// head's u and v rows by bulk copy with Q. All operand tiles use the 128-byte-swizzled
+// canonical UMMA layouts. Each softmax warp stages its 32 x 64 block of O / l in its own
+// rows of the P tile and writes it with one TMA store (rows past T are not written).
 #include <cuda.h>
 
 #include <cstdint>
@@ -293,7 +295,8 @@ __device__ __forceinline__ void bias_queries(uint8_t* smem, int row, int half) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
 parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
-                   const __grid_constant__ CUtensorMap pos_map, const T* __restrict__ ubias,
+                   const __grid_constant__ CUtensorMap pos_map,
+                   const __grid_constant__ CUtensorMap out_map, const T* __restrict__ ubias,
                    const T* __restrict__ vbias, const int32_t* __restrict__ lengths_global,
                    T* __restrict__ out, int batch, int length, int heads, float scale_log2) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -639,6 +642,12 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                     ++o_iter;
                     tc_fence_after();
                 }
+                // The item's first P overwrites the rows this warp staged the previous
+                // item's output in: that store must have read them.
+                if (j == 0) {
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+                }
                 float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                 for (int c = 0; c < kHalfKeys / 8; ++c) {
@@ -693,17 +702,16 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
             ++o_iter;
             tc_fence_after();
             const float inv = 1.0f / l_total;
-            const int row_q = it.q0 + row;
-            const bool store = row_q < length;
-            T* orow = out + (static_cast<int64_t>(it.n) * length + row_q) * C + it.h * kD +
-                      half * 64;
+            // O / l goes to this warp's own rows of the P tile (free once the last P.V has
+            // completed; the same 32 rows x 64 channels this warp writes P into), then one
+            // TMA store per warp writes them out. Rows past T fall outside the tensor map.
+            const uint32_t stage = kSmemP + half * kAtom;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t o[32];
                 tmem_ld32(tmem_row + kColO + half * 64 + c * 32, o);
                 tmem_wait_ld();
                 reg_fence(o);
-                if (!store) continue;
 #pragma unroll
                 for (int e = 0; e < 32; e += 8) {
                     const uint4 w = make_uint4(
@@ -711,16 +719,23 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                         pack2<T>(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
                         pack2<T>(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
                         pack2<T>(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
-                    *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
+                    *reinterpret_cast<uint4*>(smem + stage + sw128_offset(row, c * 4 + e / 8)) = w;
                 }
             }
             tc_fence_before();
+            fence_proxy_async_smem();
             __syncwarp();
+            if (lane == 0 && it.q0 + group * 32 < length) {
+                tma_store_3d(&out_map, sbase + stage + group * 32 * 128, it.h * kD + half * 64,
+                             it.q0 + group * 32, it.n);
+                bulk_commit_group();
+            }
             if (lane == 0) mbar_arrive(sync.bar(kBarOFree));
             item = next;
         }
     }
 
+    if (warp < kSoftmaxWarps && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == kMmaWarp) {
@@ -789,6 +804,19 @@ cudaError_t parakeet_tc_typed(const ParakeetProblem& p, cudaStream_t stream) {
             CUDA_SUCCESS)
             return cudaErrorNotSupported;
     }
+    CUtensorMap out_map;
+    {
+        const cuuint64_t dims[3] = {C, static_cast<cuuint64_t>(p.length),
+                                    static_cast<cuuint64_t>(p.batch)};
+        const cuuint64_t strides[2] = {C * sizeof(T), C * sizeof(T) * p.length};
+        const cuuint32_t box[3] = {64, 32, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (encode(&out_map, dt, 3, p.output, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS)
+            return cudaErrorNotSupported;
+    }
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(parakeet_tc_kernel<T>,
@@ -800,7 +828,7 @@ cudaError_t parakeet_tc_typed(const ParakeetProblem& p, cudaStream_t stream) {
     const int64_t items = static_cast<int64_t>((p.length + kM - 1) / kM) * p.heads * p.batch;
     const dim3 grid(static_cast<unsigned>(items < sm_count() ? items : sm_count()));
     parakeet_tc_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(
-        qkv_map, pos_map, static_cast<const T*>(p.content_bias),
+        qkv_map, pos_map, out_map, static_cast<const T*>(p.content_bias),
         static_cast<const T*>(p.position_bias), p.valid_lengths, static_cast<T*>(p.output),
         p.batch, p.length, p.heads, p.scale * kLog2e);
     return cudaGetLastError();
