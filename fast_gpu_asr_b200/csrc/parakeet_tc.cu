@@ -148,14 +148,18 @@ __device__ __forceinline__ void barrel_shift_fine(uint32_t (&v)[96], uint32_t s)
     for (int j = 0; j < 64; ++j) v[j] = (s & 1u) ? v[j + 1] : v[j];
 }
 
-template <int N> __device__ __forceinline__ float tree_max(const float (&x)[N]) {
+// Maximum of 64 values with three-input max instructions (eight independent chains).
+__device__ __forceinline__ float tree_max(const float (&x)[64]) {
     float m[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) m[i] = x[i];
+    for (int i = 0; i < 8; ++i) m[i] = fmax3(x[i], x[i + 8], x[i + 16]);
 #pragma unroll
-    for (int i = 8; i < N; ++i) m[i & 7] = fmaxf(m[i & 7], x[i]);
-    return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])),
-                 fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+    for (int i = 0; i < 8; ++i) m[i] = fmax3(m[i], x[i + 24], x[i + 32]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = fmax3(m[i], x[i + 40], x[i + 48]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], x[i + 56]);
+    return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
 struct Item {
@@ -250,9 +254,12 @@ __device__ __forceinline__ void form_logits(float (&s)[kHalfKeys],
                                             uint32_t (&band)[96], uint32_t shift, int nvalid) {
     barrel_shift_fine(band, shift);
 #pragma unroll
-    for (int e = 0; e < kHalfKeys; ++e) {
-        const float v = __uint_as_float(sc[e]) + __uint_as_float(band[e]);
-        s[e] = (!kMasked || e < nvalid) ? v : -INFINITY;
+    for (int e = 0; e < kHalfKeys; e += 2) {
+        const float2 v = f2_unpack(
+            f2_add(f2_pack(__uint_as_float(sc[e]), __uint_as_float(sc[e + 1])),
+                   f2_pack(__uint_as_float(band[e]), __uint_as_float(band[e + 1]))));
+        s[e] = (!kMasked || e < nvalid) ? v.x : -INFINITY;
+        s[e + 1] = (!kMasked || e + 1 < nvalid) ? v.y : -INFINITY;
     }
 }
 
@@ -648,22 +655,29 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                     if (lane == 0) bulk_wait_read_all();
                     __syncwarp();
                 }
-                float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                // Exponent arguments and the running sums on packed fp32 pairs.
+                const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+                const uint64_t neg_m2 = f2_pack(-m_new, -m_new);
+                uint64_t lsum2[4] = {0, 0, 0, 0};  // +0.0f pairs
 #pragma unroll
                 for (int c = 0; c < kHalfKeys / 8; ++c) {
                     uint32_t w[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float p0 = fast_exp2(fmaf(s[c * 8 + 2 * e], scale_log2, -m_new));
-                        const float p1 = fast_exp2(fmaf(s[c * 8 + 2 * e + 1], scale_log2, -m_new));
-                        lsum[e] += p0 + p1;
+                        const float2 a = f2_unpack(
+                            f2_fma(f2_pack(s[c * 8 + 2 * e], s[c * 8 + 2 * e + 1]), scale2, neg_m2));
+                        const float p0 = fast_exp2(a.x);
+                        const float p1 = fast_exp2(a.y);
+                        lsum2[e] = f2_add(lsum2[e], f2_pack(p0, p1));
                         w[e] = pack2<T>(p0, p1);
                     }
                     const uint32_t off = half * kAtom + sw128_offset(row, c);
                     *reinterpret_cast<uint4*>(smem + kSmemP + off) =
                         make_uint4(w[0], w[1], w[2], w[3]);
                 }
-                l_run = l_run * corr + ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
+                const float2 l2 = f2_unpack(f2_add(f2_add(lsum2[0], lsum2[1]),
+                                                   f2_add(lsum2[2], lsum2[3])));
+                l_run = l_run * corr + (l2.x + l2.y);
                 m_run = m_new;
                 if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
