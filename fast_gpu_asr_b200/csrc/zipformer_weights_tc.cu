@@ -244,7 +244,23 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     const uint32_t tmem = *tmem_slot;
 
     uint32_t ucount = 0;    // score-buffer uses so far (both roles count identically)
-    uint32_t kq_phase = 0;  // control warp: Q/K loads so far
+    uint32_t kq_phase = 0;  // control warp: Q/K loads waited for so far
+    int kq_pair = -1;       // control warp: pair whose Q/K loads are in flight, if any
+    // Control warp: TMA loads of Q and K of every query block of pair p.
+    auto load_qk = [&](int p) {
+        if (lane == 0) {
+            const int pn = p / heads, ph = p - pn * heads;
+            mbar_expect_tx(bar_kq, 2u * nqb * kM * kRowBytes);
+            for (int b = 0; b < nqb; ++b) {
+                tma_load_3d(sbase + kSmemQ + b * kM * kRowBytes, &proj_map, bar_kq, ph * kQd,
+                            b * kM, pn);
+                tma_load_3d(sbase + kSmemK + b * kM * kRowBytes, &proj_map, bar_kq,
+                            heads * kQd + ph * kQd, b * kM, pn);
+            }
+        }
+        __syncwarp();
+        kq_pair = p;
+    };
     // Pair tickets are drawn one pair ahead, so the atomic's round trip overlaps the work.
     if (tid == 0) next_pair[0] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
 #pragma unroll 1
@@ -264,19 +280,38 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         uint32_t* live_q = reinterpret_cast<uint32_t*>(smem + kSmemLive) + buf * 8;
 
         if (!control) {
-            // Key validity (bit per key, +-inf bias per key) and query-block liveness.
-#pragma unroll 1
-            for (int g = warp; g < ngroups; g += kComputeWarps) {
-                const int k = g * kGroup + lane;
-                const bool v = k < seq && mrow[k] == 0;
-                const uint32_t bits = __ballot_sync(0xffffffffu, v);
-                kb[k] = v ? INFINITY : -INFINITY;
-                if (lane == 0) valid[g] = bits;
+            // Key validity (bit per key, +-inf bias per key) and query-block liveness. Every
+            // mask byte a thread needs is loaded before any is used (one memory round trip).
+            constexpr int kGroupIters = (kMaxGroups + kComputeWarps - 1) / kComputeWarps;
+            uint8_t mk[kGroupIters], mq[kM / 32];
+#pragma unroll
+            for (int i = 0; i < kGroupIters; ++i) {
+                const int k = (warp + i * kComputeWarps) * kGroup + lane;
+                mk[i] = k < seq ? __ldg(mrow + k) : 1;
+            }
+#pragma unroll
+            for (int i = 0; i < kM / 32; ++i) {
+                const int q = warp * kM + lane + 32 * i;
+                mq[i] = (warp < nqb && q < seq && q >= kHalo) ? __ldg(mrow + q - kHalo) : 0;
+            }
+#pragma unroll
+            for (int i = 0; i < kGroupIters; ++i) {
+                const int g = warp + i * kComputeWarps;
+                if (g < ngroups) {
+                    const int k = g * kGroup + lane;
+                    const bool v = mk[i] == 0;
+                    const uint32_t bits = __ballot_sync(0xffffffffu, v);
+                    kb[k] = v ? INFINITY : -INFINITY;
+                    if (lane == 0) valid[g] = bits;
+                }
             }
             if (warp < nqb) {
                 bool any = false;
-                for (int q = warp * kM + lane; q < min(seq, warp * kM + kM); q += 32)
-                    any |= !(q >= kHalo && mrow[q - kHalo] != 0);
+#pragma unroll
+                for (int i = 0; i < kM / 32; ++i) {
+                    const int q = warp * kM + lane + 32 * i;
+                    any |= q < seq && mq[i] == 0;
+                }
                 any = __any_sync(0xffffffffu, any);
                 if (lane == 0) live_q[warp] = any ? 1u : 0u;
             }
@@ -295,19 +330,13 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
 
         if (control) {
             // ---- control warp: Q/K loads and the score MMAs of every live block ----
-            if (live_mask != 0u && __all_sync(0xffffffffu, *abort == 0u)) {
-                if (lane == 0) {
-                    mbar_expect_tx(bar_kq, 2u * nqb * kM * kRowBytes);
-                    for (int b = 0; b < nqb; ++b) {
-                        tma_load_3d(sbase + kSmemQ + b * kM * kRowBytes, &proj_map, bar_kq,
-                                    h * kQd, b * kM, n);
-                        tma_load_3d(sbase + kSmemK + b * kM * kRowBytes, &proj_map, bar_kq,
-                                    heads * kQd + h * kQd, b * kM, n);
-                    }
-                }
-                __syncwarp();
+            // The loads were normally issued one pair ahead (end of the previous pair).
+            if (kq_pair != pair && live_mask != 0u && __all_sync(0xffffffffu, *abort == 0u))
+                load_qk(pair);
+            if (kq_pair == pair) {
                 warp_wait(bar_kq, kq_phase & 1, abort);
                 ++kq_phase;
+                kq_pair = -1;
             }
             constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, kM, kChunk, 0, 0);
 #pragma unroll 1
@@ -334,6 +363,17 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 }
                 ucount += nchunks;
             }
+            // Once this pair's MMAs have read Q and K, load the next pair's (its ticket was
+            // drawn at the start of this pair and published by the barrier above).
+            const int nxt = next_pair[(iter + 1) & 1];
+            if (nxt < num_pairs && __all_sync(0xffffffffu, *abort == 0u)) {
+                bool ok = true;
+                if (ucount > 0) {
+                    const uint32_t u = ucount - 1;
+                    ok = warp_wait(bar_full + 8 * (u & 1), (u >> 1) & 1, abort);
+                }
+                if (ok) load_qk(nxt);
+            }
             continue;
         }
 
@@ -351,12 +391,31 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 // reads entries below 127 + 32 * ngroups.
                 const int band_lo = seq - 1 - q0 - (kM - 1);
                 const int band_fill = min(kBandFill, kM + ngroups * kGroup + 4);
-#pragma unroll 1
-                for (int i = tid; i < band_fill; i += kComputeThreads) {
+                // All of this thread's positional rows and its query's positional
+                // projection are requested before any is used (one memory round trip).
+                constexpr int kBandIters = (kBandFill + kComputeThreads - 1) / kComputeThreads;
+                uint2 raw_band[kBandIters];
+#pragma unroll
+                for (int it = 0; it < kBandIters; ++it) {
+                    const int i = tid + it * kComputeThreads;
                     const int rel = band_lo + i;
-                    uint2 raw = make_uint2(0u, 0u);
-                    if (i < seq + kM - 1 && rel >= 0 && rel < 2 * seq - 1)
-                        raw = *reinterpret_cast<const uint2*>(pos + (static_cast<int64_t>(rel) * heads + h) * 4);
+                    raw_band[it] = make_uint2(0u, 0u);
+                    if (i < band_fill && i < seq + kM - 1 && rel >= 0 && rel < 2 * seq - 1)
+                        raw_band[it] = __ldg(reinterpret_cast<const uint2*>(
+                            pos + (static_cast<int64_t>(rel) * heads + h) * 4));
+                }
+                uint2 raw_pq = make_uint2(0u, 0u);
+                uint8_t halo_mask = 0;
+                if (q < seq) {
+                    raw_pq = __ldg(reinterpret_cast<const uint2*>(
+                        proj + (static_cast<int64_t>(n) * seq + q) * pdim + 2 * heads * kQd + h * 4));
+                    if (q >= kHalo) halo_mask = __ldg(mrow + q - kHalo);
+                }
+#pragma unroll
+                for (int it = 0; it < kBandIters; ++it) {
+                    const int i = tid + it * kComputeThreads;
+                    if (i >= band_fill) break;
+                    const uint2 raw = raw_band[it];
                     const uint16_t v[4] = {static_cast<uint16_t>(raw.x & 0xFFFFu),
                                            static_cast<uint16_t>(raw.x >> 16),
                                            static_cast<uint16_t>(raw.y & 0xFFFFu),
@@ -372,13 +431,12 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 }
                 uint16_t pq[4] = {0, 0, 0, 0};
                 if (q < seq) {
-                    const uint2 raw = *reinterpret_cast<const uint2*>(
-                        proj + (static_cast<int64_t>(n) * seq + q) * pdim + 2 * heads * kQd + h * 4);
+                    const uint2 raw = raw_pq;
                     pq[0] = static_cast<uint16_t>(raw.x & 0xFFFFu);
                     pq[1] = static_cast<uint16_t>(raw.x >> 16);
                     pq[2] = static_cast<uint16_t>(raw.y & 0xFFFFu);
                     pq[3] = static_cast<uint16_t>(raw.y >> 16);
-                    row_live = !(q >= kHalo && mrow[q - kHalo] != 0);
+                    row_live = halo_mask == 0;
                 }
                 const bool warp_live = __any_sync(0xffffffffu, row_live);
                 named_barrier(3, kComputeThreads);  // band complete
@@ -592,11 +650,15 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         }
     }
 
-    // Teardown: the control warp waits (bounded) for its last MMA before TMEM is freed.
+    // Teardown: the control warp waits (bounded) for its last MMA before TMEM is freed,
+    // and for Q/K loads still in flight (only after an abort) before shared memory is.
     if (control && ucount > 0) {
         const uint32_t u = ucount - 1;
         if (!mbar_wait(bar_full + 8 * (u & 1), (u >> 1) & 1) && lane == 0)
             atomicExch(&g_zipformer_tc_error, 1u);
+    }
+    if (control && kq_pair >= 0) {
+        if (!mbar_wait(bar_kq, kq_phase & 1) && lane == 0) atomicExch(&g_zipformer_tc_error, 1u);
     }
     tc_fence_before();
     __syncthreads();
