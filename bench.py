@@ -1,7 +1,7 @@
 """Encoder-attention benchmark: audio-seconds per second through the attention plugins.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload parakeet|parakeet_long|zipformer|ragged]
+                    [--workload parakeet|parakeet_long|zipformer|zipformer_fused|ragged]
     python bench.py --impl reference ...   # the reference math on the host cores
 
 A *step* is one encoder forward's worth of attention calls over one batch:
@@ -48,7 +48,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("parakeet", "parakeet_long", "zipformer", "ragged"),
+    p.add_argument("--workload", choices=("parakeet", "parakeet_long", "zipformer",
+                                          "zipformer_fused", "ragged"),
                    default="parakeet")
     p.add_argument("--batch", type=int, default=None,
                    help="utterances per GPU (default 256; 16 for parakeet_long)")
@@ -233,7 +234,7 @@ def run_parakeet_step(layers, outs, stream, events=None):
             events[i][1].record(stream)
 
 
-def build_zipformer(args, rank):
+def build_zipformer(args, rank, fused=False):
     import torch
 
     from fast_gpu_asr_b200 import workloads as wl
@@ -253,9 +254,47 @@ def build_zipformer(args, rank):
             layers.append(L)
             total_bytes += wl.zipformer_layer_bytes(args.batch, t, embed, heads, 2)
         outs = (torch.empty_like(layers[0].value_a), torch.empty_like(layers[0].nonlin_value))
+        if fused:
+            # The fused entry point writes head 0's weights only, and both self outputs.
+            weights = torch.empty((args.batch, 1, t, t), dtype=torch.bfloat16, device="cuda")
+            outs = outs + (torch.empty_like(layers[0].value_b),)
         stacks.append((heads, weights, layers, outs))
     torch.cuda.synchronize()
     return stacks, wl.zipformer_audio_seconds(input_lengths), total_bytes
+
+
+def zipformer_fused_launch_bytes(stacks):
+    """(call, algorithmic bytes, kernels) of every call of one fused step, in call order."""
+    out = []
+    for heads, weights0, layers, (out_a, out_nl, out_b) in stacks:
+        for L in layers:
+            n, t = L.projection.shape[:2]
+            w0 = n * t * t * 2
+            out.append(("zipformer_attention_fused",
+                        L.projection.numel() * 2 + L.position.numel() * 2 + L.mask.numel()
+                        + 2 * L.value_a.numel() * 2 + 2 * out_a.numel() * 2 + w0, 2))
+            out.append(("zipformer_attention_value",
+                        w0 + L.nonlin_value.numel() * 2 + out_nl.numel() * 2, 1))
+    return out
+
+
+def run_zipformer_fused_step(stacks, stream, events=None):
+    from fast_gpu_asr_b200.attention import zipformer_attention_fused, zipformer_attention_value
+
+    j = 0
+    for heads, weights0, layers, (out_a, out_nl, out_b) in stacks:
+        for L in layers:
+            if events is not None:
+                events[j][0].record(stream)
+            zipformer_attention_fused(L.projection, L.position, L.mask, L.value_a, L.value_b,
+                                      out1=out_a, out2=out_b, weights0=weights0, stream=stream)
+            if events is not None:
+                events[j][1].record(stream)
+                events[j + 1][0].record(stream)
+            zipformer_attention_value(weights0, L.nonlin_value, 1, out=out_nl, stream=stream)
+            if events is not None:
+                events[j + 1][1].record(stream)
+            j += 2
 
 
 def zipformer_launch_bytes(stacks):
@@ -410,6 +449,14 @@ def workload_config(args) -> dict:
                 "frames": 375, "heads": 8, "head_dim": 128, "layers": 24,
                 "lengths": "U[60,375]", "dtype": "f16", "parallelism": f"dp{args.gpus}",
                 "l2": "inputs exceed L2 (590 MB QKV per layer, 24 distinct layers)"}
+    if args.workload == "zipformer_fused":
+        return {"workload": "zipformer fused weights + both self-attention values, then the "
+                            "nonlinear attention-value call on head 0's weights, per layer "
+                            "(config 3 through zipformer_attention_fused: beyond the drop-in "
+                            "surface)",
+                "batch": args.batch, "stacks_T": [750, 375, 188, 94, 188, 375],
+                "layers": [2, 2, 4, 5, 4, 2], "dtype": "bf16", "parallelism": f"dp{args.gpus}",
+                "l2": "per-layer inputs of distinct layers; head-0 weights up to 288 MB"}
     if args.workload == "ragged":
         return {"workload": "ragged whole-box run (config 5): 20,000 lognormal utterances, "
                             "length-sorted batches of 256 dealt round-robin; per batch 24 "
@@ -523,6 +570,15 @@ def ours_arm(args, world, rank, local):
 
         def step(events=None):
             run_parakeet_step(layers, outs, stream, events)
+    elif args.workload == "zipformer_fused":
+        stacks, audio, _ = build_zipformer(args, rank, fused=True)
+        calls = zipformer_fused_launch_bytes(stacks)
+        launch_kinds = [(name, nb) for name, nb, _ in calls]
+        kernels_per_step = sum(k for _, _, k in calls)
+        total_bytes = float(sum(nb for _, nb in launch_kinds))
+
+        def step(events=None):
+            run_zipformer_fused_step(stacks, stream, events)
     else:
         stacks, audio, total_bytes = build_zipformer(args, rank)
         launch_kinds = zipformer_launch_bytes(stacks)
@@ -530,6 +586,8 @@ def ours_arm(args, world, rank, local):
         def step(events=None):
             run_zipformer_step(stacks, stream, events)
     n_launch = len(launch_kinds)
+    if args.workload != "zipformer_fused":
+        kernels_per_step = n_launch
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -605,14 +663,15 @@ def ours_arm(args, world, rank, local):
                     "step_hbm_frac": total_bytes / (ms_per_step / 1000.0) / 1e9
                     / peaks["hbm_gbs"],
                     "variant": variant}
-    gpu_launches = args.steps * n_launch
+    gpu_launches = args.steps * kernels_per_step
 
     e2e = None
     if not args.no_e2e:
         if is_parakeet(args):
             e2e = e2e_parakeet(args, layers, audio, world)
         else:
-            e2e = e2e_zipformer(args, stacks, audio, world)
+            e2e = e2e_zipformer(args, stacks, audio, world,
+                                fused=args.workload == "zipformer_fused")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -724,22 +783,27 @@ def e2e_parakeet(args, layers, audio, world):
             "ms_per_step": ms / n, "overlap": "copy-in, compute and copy-out streams"}
 
 
-def e2e_zipformer(args, stacks, audio, world):
+def e2e_zipformer(args, stacks, audio, world, fused=False):
     """Same metric through the public API with pinned host inputs and outputs.
 
     Per layer the step copies in the projection, positions, mask and the three value
-    inputs, runs the weights call and the three attention-value calls, and copies the
-    three attention outputs back. The NHTT weights stay on the device, as between two
-    plugins of an engine. Copies overlap compute across layers (three-stream pipeline).
+    inputs, runs the weights call and the three attention-value calls (fused: the fused
+    call and the nonlinear attention-value call), and copies the three attention outputs
+    back. The weights stay on the device, as between two plugins of an engine. Copies
+    overlap compute across layers (three-stream pipeline).
     """
     import torch
 
-    from fast_gpu_asr_b200.attention import zipformer_attention_value, zipformer_relative_attention
+    from fast_gpu_asr_b200.attention import (
+        zipformer_attention_fused,
+        zipformer_attention_value,
+        zipformer_relative_attention,
+    )
 
     names = ("projection", "position", "mask", "value_a", "value_b", "nonlin_value")
     plan = []  # one entry per layer call: (heads, weights, host, dev[2], outs[2], host_outs[2])
     h2d_bytes = d2h_bytes = 0
-    for heads, weights, layers, (out_self, out_nl) in stacks:
+    for heads, weights, layers, (out_self, out_nl, *_) in stacks:
         L0 = layers[0]
         host = {k: getattr(L0, k).cpu().pin_memory() for k in names}
         dev = [{k: torch.empty_like(getattr(L0, k)) for k in names} for _ in range(2)]
@@ -760,6 +824,12 @@ def e2e_zipformer(args, stacks, audio, world):
     def compute(i, b, s):
         heads, weights, host, dev, outs, host_outs = plan[i]
         d, o = dev[b], outs[b]
+        if fused:
+            zipformer_attention_fused(d["projection"], d["position"], d["mask"], d["value_a"],
+                                      d["value_b"], out1=o[0], out2=o[1], weights0=weights,
+                                      stream=s)
+            zipformer_attention_value(weights, d["nonlin_value"], 1, out=o[2], stream=s)
+            return
         zipformer_relative_attention(d["projection"], d["position"], d["mask"], out=weights,
                                      stream=s)
         zipformer_attention_value(weights, d["value_a"], heads, out=o[0], stream=s)

@@ -9,6 +9,7 @@ data-parallel batch-sharding launcher.
 
 from .attention import (  # noqa: F401
     parakeet_relative_attention,
+    zipformer_attention_fused,
     zipformer_attention_value,
     zipformer_relative_attention,
 )

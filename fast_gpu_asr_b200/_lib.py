@@ -31,6 +31,7 @@ STATUS_NAMES = {
     6: "FGA_ERROR_PRIOR_CUDA_ERROR",
     7: "FGA_ERROR_LAUNCH",
     8: "FGA_ERROR_NO_DEVICE",
+    9: "FGA_ERROR_UNSUPPORTED",
 }
 
 
@@ -81,6 +82,10 @@ SYMBOLS = {
         ctypes.c_int32,
         (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.c_int32, _VP,
          ctypes.c_size_t, _VP)),
+    "fga_zipformer_attention_fused_check": (
+        ctypes.c_int32, (_P, ctypes.c_int32, _P, ctypes.c_int32)),
+    "fga_zipformer_attention_fused_enqueue": (
+        ctypes.c_int32, (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP)),
     "fga_abi_version": (ctypes.c_int32, ()),
     "fga_status_string": (ctypes.c_char_p, (ctypes.c_int32,)),
     "fga_last_kernel_variant": (ctypes.c_char_p, ()),

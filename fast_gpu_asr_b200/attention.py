@@ -10,6 +10,10 @@ ONNX nodes its export modules emit):
 * ``zipformer_attention_value(attention, value, num_heads)`` -
   ``export/model/zipformer/attention.py:62-73, 130-138``
 
+One more operator has no reference plugin: ``zipformer_attention_fused`` applies the
+Zipformer weights to both SelfAttention value tensors in one kernel, without writing the
+``[N, H, T, T]`` weights (it returns head 0's weights for NonlinAttention).
+
 Error behaviour follows the plugins: a binding whose shape, rank or dtype violates the
 contract is rejected before anything is launched (``AttentionError`` with the C ABI's
 status), and a pending CUDA error from earlier work is reported, not hidden. Tensors
@@ -143,3 +147,44 @@ def zipformer_attention_value(attention: torch.Tensor, value: torch.Tensor, num_
         ins, outs, in_ptrs, out_ptrs, int(num_heads), None, 0, _stream_handle(stream))
     _check(status, "zipformer_attention_value")
     return out
+
+
+def zipformer_attention_fused_check(input_descs, output_descs) -> int:
+    lib = _lib.library()
+    ins = _lib.desc_array(input_descs)
+    outs = _lib.desc_array(output_descs)
+    return lib.fga_zipformer_attention_fused_check(ins, len(input_descs), outs, len(output_descs))
+
+
+def zipformer_attention_fused(projection: torch.Tensor, position: torch.Tensor,
+                              mask: torch.Tensor, value1: torch.Tensor, value2: torch.Tensor, *,
+                              out1: torch.Tensor | None = None, out2: torch.Tensor | None = None,
+                              weights0: torch.Tensor | None = None, stream=None):
+    """``(out1, out2, weights0)``: ``zipformer_attention_value(W, value_i, H)`` for the
+    weights ``W = zipformer_relative_attention(projection, position, mask)``, and
+    ``W[:, :1]``, without materialising ``W``.
+
+    Tensor-core path only (f16/bf16, query dim 32, an even number of heads, T <= 768,
+    value head dim a multiple of 4 up to 16); other problems raise ``AttentionError``
+    with FGA_ERROR_UNSUPPORTED.
+    """
+    lib = _lib.library()
+    n, t = projection.shape[0], projection.shape[1]
+    if out1 is None:
+        out1 = torch.empty_like(value1)
+    if out2 is None:
+        out2 = torch.empty_like(value2)
+    if weights0 is None:
+        weights0 = torch.empty((n, 1, t, t), dtype=projection.dtype, device=projection.device)
+    tensors = (projection, position, mask, value1, value2)
+    names = ("projection", "position", "mask", "value1", "value2")
+    outputs = (out1, out2, weights0)
+    ins = _lib.desc_array([_desc(x) for x in tensors])
+    outs = _lib.desc_array([_desc(x) for x in outputs])
+    in_ptrs = _lib.pointer_array([_ptr(x, nm) for x, nm in zip(tensors, names)])
+    out_ptrs = _lib.pointer_array(
+        [_ptr(x, nm) for x, nm in zip(outputs, ("out1", "out2", "weights0"))])
+    status = lib.fga_zipformer_attention_fused_enqueue(
+        ins, outs, in_ptrs, out_ptrs, _stream_handle(stream))
+    _check(status, "zipformer_attention_fused")
+    return out1, out2, weights0

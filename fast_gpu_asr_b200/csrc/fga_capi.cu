@@ -173,6 +173,56 @@ int32_t check_value(const fga_tensor_desc* in, int32_t nin, const fga_tensor_des
     return FGA_SUCCESS;
 }
 
+// The fused Zipformer entry point: the weights contract of check_zipformer on inputs
+// 0..2, two value tensors and two outputs [N, T, H*vd], head 0's weights [N, 1, T, T],
+// then the tensor-core envelope (FGA_ERROR_UNSUPPORTED outside it).
+int32_t check_fused(const fga_tensor_desc* in, int32_t nin, const fga_tensor_desc* out,
+                    int32_t nout, fga::ZipformerFusedProblem* prob) {
+    if (in == nullptr || out == nullptr) return FGA_ERROR_NULL_POINTER;
+    if (nin != 5 || nout != 3) return FGA_ERROR_BAD_DESCRIPTOR;
+    const fga_tensor_desc &proj = in[0], &pos = in[1], &v1 = in[3], &v2 = in[4];
+    if (proj.nb_dims != 3 || pos.nb_dims != 4) return FGA_ERROR_BAD_DESCRIPTOR;
+    // The weights contract, checked against the [N, H, T, T] tensor it would produce.
+    fga_tensor_desc weights{};
+    weights.type = proj.type;
+    weights.nb_dims = 4;
+    weights.dims[0] = proj.dims[0];
+    weights.dims[1] = pos.dims[2];
+    weights.dims[2] = proj.dims[1];
+    weights.dims[3] = proj.dims[1];
+    fga::ZipformerWeightsProblem w{};
+    int32_t st = check_zipformer(in, 3, &weights, 1, &w);
+    if (st != FGA_SUCCESS) return st;
+    const int32_t t = proj.type;
+    for (const fga_tensor_desc* d : {&v1, &v2, &out[0], &out[1]})
+        if (d->nb_dims != 3 || d->type != t) return FGA_ERROR_BAD_DESCRIPTOR;
+    if (out[2].nb_dims != 4 || out[2].type != t) return FGA_ERROR_BAD_DESCRIPTOR;
+    for (const fga_tensor_desc* d : {&v1, &v2, &out[0], &out[1], &out[2]})
+        if (!addressable(*d, true)) return FGA_ERROR_OVERFLOW;
+    const int64_t n = proj.dims[0], len = proj.dims[1], heads = w.heads;
+    for (const fga_tensor_desc* d : {&v2, &out[0], &out[1]})
+        if (d->dims[0] != v1.dims[0] || d->dims[1] != v1.dims[1] || d->dims[2] != v1.dims[2])
+            return FGA_ERROR_BAD_SHAPE;
+    if (v1.dims[0] != n || v1.dims[1] != len || v1.dims[2] % heads != 0 ||
+        out[2].dims[0] != n || out[2].dims[1] != 1 || out[2].dims[2] != len ||
+        out[2].dims[3] != len)
+        return FGA_ERROR_BAD_SHAPE;
+    const int64_t vd = v1.dims[2] / heads;
+    // Projection and value rows are read by TMA: 16-byte multiples (an even H for qd = 32).
+    if ((t != FGA_HALF && t != FGA_BF16) || w.query_dim != 32 || len > 768 || vd < 4 ||
+        vd > 16 || vd % 4 != 0 || (heads * vd * 2) % 16 != 0 || (heads * 68 * 2) % 16 != 0)
+        return FGA_ERROR_UNSUPPORTED;
+    if (prob != nullptr) {
+        prob->batch = w.batch;
+        prob->length = w.length;
+        prob->heads = w.heads;
+        prob->query_dim = w.query_dim;
+        prob->value_dim = static_cast<int32_t>(vd);
+        prob->dtype = t;
+    }
+    return FGA_SUCCESS;
+}
+
 // Common epilogue of every enqueue: report an earlier asynchronous error without
 // launching (parakeet…cu:948-952), launch, report the launch status.
 int32_t prior_error_status() {
@@ -196,6 +246,7 @@ const char* fga_status_string(int32_t status) {
         case FGA_ERROR_PRIOR_CUDA_ERROR: return "an earlier CUDA error is pending";
         case FGA_ERROR_LAUNCH: return "kernel launch failed";
         case FGA_ERROR_NO_DEVICE: return "current CUDA device is not sm_100";
+        case FGA_ERROR_UNSUPPORTED: return "outside this entry point's supported envelope";
         default: return "unknown status";
     }
 }
@@ -306,6 +357,41 @@ int32_t fga_zipformer_attention_value_enqueue(const fga_tensor_desc* in,
     cudaError_t e = fga::launch_zipformer_value(p, static_cast<cudaStream_t>(stream), &variant);
     if (e != cudaSuccess) return FGA_ERROR_LAUNCH;
     t_last_variant = variant;
+    return FGA_SUCCESS;
+}
+
+// ---- zipformer fused weights + attention-value -------------------------------------------
+int32_t fga_zipformer_attention_fused_check(const fga_tensor_desc* in, int32_t nin,
+                                            const fga_tensor_desc* out, int32_t nout) {
+    return check_fused(in, nin, out, nout, nullptr);
+}
+
+int32_t fga_zipformer_attention_fused_enqueue(const fga_tensor_desc* in,
+                                              const fga_tensor_desc* out,
+                                              const void* const* inputs, void* const* outputs,
+                                              void* stream) {
+    fga::ZipformerFusedProblem p{};
+    int32_t st = check_fused(in, 5, out, 3, &p);
+    if (st != FGA_SUCCESS) return st;
+    if (inputs == nullptr || outputs == nullptr) return FGA_ERROR_NULL_POINTER;
+    for (int i = 0; i < 5; ++i)
+        if (inputs[i] == nullptr) return FGA_ERROR_NULL_POINTER;
+    for (int i = 0; i < 3; ++i)
+        if (outputs[i] == nullptr) return FGA_ERROR_NULL_POINTER;
+    if ((st = prior_error_status()) != FGA_SUCCESS) return st;
+    if (!fga::device_is_sm100()) return FGA_ERROR_NO_DEVICE;
+    p.projection = inputs[0];
+    p.position = inputs[1];
+    p.mask = static_cast<const uint8_t*>(inputs[2]);
+    p.value1 = inputs[3];
+    p.value2 = inputs[4];
+    p.output1 = outputs[0];
+    p.output2 = outputs[1];
+    p.weights0 = outputs[2];
+    const cudaError_t e = fga::launch_zipformer_fused(p, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorNotSupported) return FGA_ERROR_UNSUPPORTED;  // buffer alignment
+    if (e != cudaSuccess) return FGA_ERROR_LAUNCH;
+    t_last_variant = "tcgen05";
     return FGA_SUCCESS;
 }
 

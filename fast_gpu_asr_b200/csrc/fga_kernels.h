@@ -25,8 +25,24 @@ struct ZipformerWeightsProblem {
     const void* projection;  // [N, T, H*(2qd+4)]
     const void* position;    // [1, 2T-1, H, 4]
     const uint8_t* mask;     // [N, T] bool
-    void* weights;           // [N, H, T, T]
+    void* weights;           // [N, out_heads, T, T]
     int32_t batch, length, heads, query_dim;
+    int32_t dtype;
+    int32_t out_heads = 0;   // heads [0, out_heads) are computed; 0 means all H
+};
+
+// Zipformer weights applied in the same kernel to the two SelfAttention value tensors
+// (no [N, H, T, T] tensor is written), plus head 0's weights for NonlinAttention.
+struct ZipformerFusedProblem {
+    const void* projection;  // [N, T, H*(2qd+4)]
+    const void* position;    // [1, 2T-1, H, 4]
+    const uint8_t* mask;     // [N, T] bool
+    const void* value1;      // [N, T, H*vd]
+    const void* value2;      // [N, T, H*vd]
+    void* output1;           // [N, T, H*vd]
+    void* output2;           // [N, T, H*vd]
+    void* weights0;          // [N, 1, T, T]: head 0's weights
+    int32_t batch, length, heads, query_dim, value_dim;
     int32_t dtype;
 };
 
@@ -44,6 +60,9 @@ cudaError_t launch_zipformer_weights(const ZipformerWeightsProblem& p, cudaStrea
                                      const char** variant);
 cudaError_t launch_zipformer_value(const ZipformerValueProblem& p, cudaStream_t stream,
                                    const char** variant);
+// Tensor cores only: cudaErrorNotSupported outside the envelope (f16/bf16, qd = 32,
+// T <= 768, vd a multiple of 4 up to 16, H*vd a multiple of 8, aligned buffers).
+cudaError_t launch_zipformer_fused(const ZipformerFusedProblem& p, cudaStream_t stream);
 
 // SIMT (CUDA-core) kernels: every dtype and shape the contract accepts.
 cudaError_t launch_parakeet_simt(const ParakeetProblem& p, cudaStream_t stream);

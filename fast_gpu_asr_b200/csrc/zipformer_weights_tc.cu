@@ -81,20 +81,40 @@ constexpr int kStageWarp = 32 * kStageRow;
 // pairs round-robin; the last CTA of a launch resets its pair to zero.
 constexpr int kSchedSlots = 64;
 
-// Shared memory (bytes from the 1024-aligned base).
+// Fused variant (weights applied to two value tensors in the same kernel): pass 2 writes
+// each 64-key piece of rounded weights into a P tile (one per warp sub-slot, 128 rows x
+// 64 keys, SWIZZLE_128B K-major) and the control warp multiplies it by the head's V
+// pieces, which stay resident for the whole pair (64 keys x 16 channels per piece,
+// SWIZZLE_32B MN-major, both value tensors).
+constexpr uint32_t kPTile = kM * kPiece * 2;
+constexpr uint32_t kVPiece = kPiece * 16 * 2;
+constexpr int kVBox = 256;  // keys per V TMA box (four pieces)
+constexpr uint32_t kVTensor = (kMaxT / kPiece) * kVPiece;
+
+// Shared memory (bytes from the 1024-aligned base). The variant region holds the pass-2
+// staging tiles (weights kernel) or the P tiles and resident V (fused kernel).
 constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemK = kSmemQ + kMaxT * kRowBytes;
 constexpr uint32_t kSmemBand = kSmemK + kMaxT * kRowBytes;
-constexpr uint32_t kSmemStage = kSmemBand + 4u * kCopy * 2u;
-constexpr uint32_t kSmemHist = kSmemStage + kComputeWarps * kStageWarp + 16;
+constexpr uint32_t kSmemHist = kSmemBand + 4u * kCopy * 2u;
 constexpr uint32_t kSmemStats = kSmemHist + kMaxGroups * kM * 4;
 constexpr uint32_t kSmemKb = kSmemStats + kSub * kM * 8;          // 2 buffers (pair parity)
 constexpr uint32_t kSmemValid = kSmemKb + 2 * kMaxT * 4;           // 2 buffers
 constexpr uint32_t kSmemLive = kSmemValid + 2 * kMaxGroups * 4;    // 2 buffers x 8 words
-constexpr uint32_t kSmemBar = kSmemLive + 2 * 8 * 4;
-constexpr uint32_t kSmemBytes = kSmemBar + 64;
+constexpr uint32_t kSmemVariant = (kSmemLive + 2 * 8 * 4 + 1023u) & ~1023u;
+constexpr uint32_t kSmemStage = kSmemVariant;
+constexpr uint32_t kSmemP = kSmemVariant;
+constexpr uint32_t kSmemV = kSmemP + kSub * kPTile;  // value v at + v * kVTensor
+template <bool kFused> struct SmemEnd {
+    // Barriers: [0, 64) shared by both variants; fused adds a_full[2], a_empty[2], v_full,
+    // o_full, o_free at [64, 120).
+    static constexpr uint32_t bar =
+        kFused ? kSmemV + 2 * kVTensor : kSmemStage + kComputeWarps * kStageWarp + 16;
+    static constexpr uint32_t bytes = bar + (kFused ? 128u : 64u);
+};
 static_assert(kCopy % 64 == 16, "band copy stride");
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(SmemEnd<false>::bytes <= 227 * 1024 && SmemEnd<true>::bytes <= 227 * 1024,
+              "shared memory budget");
 static_assert(kMaxT / kM <= kComputeWarps, "one warp per query block computes its liveness");
 
 __device__ unsigned int g_zipformer_tc_error = 0;
@@ -187,13 +207,20 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
     return ok;
 }
 
-template <typename T>
+// kFused = false: attention weights of heads [0, out_heads) written as [N, out_heads, T, T].
+// kFused = true: the weights of every head (out_heads == heads) applied to two value
+// tensors [N, T, heads * vd] (v1_map, v2_map) into out1 and out2; nothing else is written.
+template <typename T, bool kFused>
 __global__ void __launch_bounds__(kThreads, 1)
 zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
+                            const __grid_constant__ CUtensorMap v1_map,
+                            const __grid_constant__ CUtensorMap v2_map,
                             const T* __restrict__ proj, const T* __restrict__ pos,
-                            const uint8_t* __restrict__ mask, T* __restrict__ out, int seq,
-                            int heads, int num_pairs, int slot) {
+                            const uint8_t* __restrict__ mask, T* __restrict__ out,
+                            T* __restrict__ out1, T* __restrict__ out2, int seq, int heads,
+                            int out_heads, int vd, int num_pairs, int slot) {
     extern __shared__ __align__(1024) uint8_t smem[];
+    constexpr uint32_t kSmemBar = SmemEnd<kFused>::bar;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar_kq = sbase + kSmemBar;
     const uint32_t bar_full = sbase + kSmemBar + 8;   // + 8 * buffer
@@ -202,6 +229,12 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + kSmemBar + 44);
     uint16_t* band = reinterpret_cast<uint16_t*>(smem + kSmemBand);
     volatile int* next_pair = reinterpret_cast<volatile int*>(smem + kSmemBar + 48);  // [2]
+    // Fused variant only.
+    const uint32_t bar_a_full = sbase + kSmemBar + 64;    // + 8 * sub-slot
+    const uint32_t bar_a_empty = sbase + kSmemBar + 80;   // + 8 * sub-slot
+    const uint32_t bar_v_full = sbase + kSmemBar + 96;
+    const uint32_t bar_o_full = sbase + kSmemBar + 104;
+    const uint32_t bar_o_free = sbase + kSmemBar + 112;
     float* hist = reinterpret_cast<float*>(smem + kSmemHist);
     float2* stats = reinterpret_cast<float2*>(smem + kSmemStats);
 
@@ -230,6 +263,17 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         mbar_init(bar_full + 8, 1);
         mbar_init(bar_free, kComputeWarps);
         mbar_init(bar_free + 8, kComputeWarps);
+        if constexpr (kFused) {
+            for (int i = 0; i < kSub; ++i) {
+                mbar_init(bar_a_full + 8 * i, 4);  // the sub-slot's four warps
+                mbar_init(bar_a_empty + 8 * i, 1);
+            }
+            mbar_init(bar_v_full, 1);
+            mbar_init(bar_o_full, 1);
+            mbar_init(bar_o_free, kComputeWarps);
+            prefetch_tensormap(&v1_map);
+            prefetch_tensormap(&v2_map);
+        }
         *abort = 0u;
         fence_mbar_init();
         prefetch_tensormap(&proj_map);
@@ -244,12 +288,20 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     const uint32_t tmem = *tmem_slot;
 
     uint32_t ucount = 0;    // score-buffer uses so far (both roles count identically)
+    // Fused variant: P-tile uses per sub-slot (both roles count identically), the control
+    // warp's o_full commits / o_free and v_full waits, and the score buffer holding the
+    // accumulators of an output tile whose epilogue has not been waited for (-1: none).
+    uint32_t a_uses[kSub] = {0, 0};  // control warp
+    uint32_t p_uses = 0;             // compute warp: P tiles of its sub-slot written
+    uint32_t o_fulls = 0, o_frees = 0, v_waits = 0;
+    int o_buf = -1;
+    bool v_pending = false;
     uint32_t kq_phase = 0;  // control warp: Q/K loads waited for so far
     int kq_pair = -1;       // control warp: pair whose Q/K loads are in flight, if any
     // Control warp: TMA loads of Q and K of every query block of pair p.
     auto load_qk = [&](int p) {
         if (lane == 0) {
-            const int pn = p / heads, ph = p - pn * heads;
+            const int pn = p / out_heads, ph = p - pn * out_heads;
             mbar_expect_tx(bar_kq, 2u * nqb * kM * kRowBytes);
             for (int b = 0; b < nqb; ++b) {
                 tma_load_3d(sbase + kSmemQ + b * kM * kRowBytes, &proj_map, bar_kq, ph * kQd,
@@ -271,8 +323,8 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         // Every thread read slot (iter+1)&1 of the previous pair before this barrier.
         if (tid == 0)
             next_pair[(iter + 1) & 1] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
-        const int n = pair / heads;
-        const int h = pair - n * heads;
+        const int n = pair / out_heads;
+        const int h = pair - n * out_heads;
         const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
         const int buf = iter & 1;
         float* kb = reinterpret_cast<float*>(smem + kSmemKb) + buf * kMaxT;
@@ -338,6 +390,29 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 ++kq_phase;
                 kq_pair = -1;
             }
+            if constexpr (kFused) {
+                // The head's V pieces of both value tensors, resident for the pair, once the
+                // previous pair's last P.V MMAs have read theirs. They land under pass 1.
+                if (live_mask != 0u && __all_sync(0xffffffffu, *abort == 0u)) {
+                    bool ok = true;
+                    if (o_fulls > 0) ok = warp_wait(bar_o_full, (o_fulls - 1) & 1, abort);
+                    if (ok) {
+                        if (lane == 0) {
+                            const int nvb = (seq + kVBox - 1) / kVBox;
+                            const int cb = (h * vd) & ~7;
+                            mbar_expect_tx(bar_v_full, 2u * nvb * kVBox * 32u);
+                            for (int vb = 0; vb < nvb; ++vb) {
+                                tma_load_3d(sbase + kSmemV + vb * kVBox * 32u, &v1_map,
+                                            bar_v_full, cb, vb * kVBox, n);
+                                tma_load_3d(sbase + kSmemV + kVTensor + vb * kVBox * 32u,
+                                            &v2_map, bar_v_full, cb, vb * kVBox, n);
+                            }
+                        }
+                        __syncwarp();
+                        v_pending = true;
+                    }
+                }
+            }
             constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, kM, kChunk, 0, 0);
 #pragma unroll 1
             for (int b = 0; b < nqb; ++b) {
@@ -349,6 +424,14 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     const uint32_t sb = u & 1;
                     bool ok = __all_sync(0xffffffffu, *abort == 0u);
                     if (ok && u >= 2) ok = warp_wait(bar_free + 8 * sb, ((u >> 1) - 1) & 1, abort);
+                    if constexpr (kFused) {
+                        // This buffer holds the accumulators of an earlier output tile.
+                        if (ok && static_cast<int>(sb) == o_buf) {
+                            ok = warp_wait(bar_o_free, o_frees & 1, abort);
+                            ++o_frees;
+                            o_buf = -1;
+                        }
+                    }
                     if (ok) {
                         tc_fence_after();
                         if (elect_one()) {
@@ -362,6 +445,63 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     }
                 }
                 ucount += nchunks;
+                if constexpr (kFused) {
+                    // P.V of this block: O1, O2 (16 columns each) accumulate in the score
+                    // buffer of the block's last chunk, which pass 1 has drained by the
+                    // time the first P tile is full. Steps alternate the two sub-slots.
+                    constexpr uint32_t idesc_pv = idesc_f16(Fmt<T>::v, kM, 16, 0, 1);
+                    bool ok = __all_sync(0xffffffffu, *abort == 0u);
+                    if (ok && o_buf >= 0) {
+                        ok = warp_wait(bar_o_free, o_frees & 1, abort);
+                        ++o_frees;
+                        o_buf = -1;
+                    }
+                    if (ok && v_pending) {
+                        ok = warp_wait(bar_v_full, v_waits & 1, abort);
+                        ++v_waits;
+                        v_pending = false;
+                    }
+                    const uint32_t ob = (ucount & 1u) ^ 1u;
+                    const int cnt[kSub] = {split, npieces - split};
+                    const int steps = max(cnt[0], cnt[1]);
+                    bool first = true;
+#pragma unroll 1
+                    for (int i = 0; i < steps; ++i) {
+#pragma unroll
+                        for (int sl = 0; sl < kSub; ++sl) {
+                            if (i >= cnt[sl]) continue;
+                            const int piece = sl == 0 ? i : split + i;
+                            if (ok) ok = warp_wait(bar_a_full + 8 * sl, a_uses[sl] & 1, abort);
+                            if (ok) {
+                                tc_fence_after();
+                                if (elect_one()) {
+                                    const uint64_t da =
+                                        sw128_desc(sbase + kSmemP + sl * kPTile, 16, 1024);
+#pragma unroll
+                                    for (int v = 0; v < 2; ++v) {
+                                        const uint64_t dv = smem_desc(
+                                            sbase + kSmemV + v * kVTensor + piece * kVPiece,
+                                            kVPiece, 256, 6);
+#pragma unroll
+                                        for (uint32_t ks = 0; ks < kPiece / 16; ++ks)
+                                            umma_f16_ss(tmem + ob * kChunk + v * 16,
+                                                        da + ((ks * 32) >> 4),
+                                                        dv + ((ks * 512) >> 4), idesc_pv,
+                                                        (first && ks == 0) ? 0u : 1u);
+                                    }
+                                    umma_commit(bar_a_empty + 8 * sl);
+                                }
+                                __syncwarp();
+                            }
+                            ++a_uses[sl];
+                            first = false;
+                        }
+                    }
+                    if (elect_one()) umma_commit(bar_o_full);
+                    __syncwarp();
+                    ++o_fulls;
+                    o_buf = static_cast<int>(ob);
+                }
             }
             // Once this pair's MMAs have read Q and K, load the next pair's (its ticket was
             // drawn at the start of this pair and published by the barrier above).
@@ -543,6 +683,21 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 row_live = row_live && inv > 0.0f;
             }
 
+            // Fused: this warp's value tensor (sub-slot 0: first, 1: second) and its output
+            // row; the head's vd channels start `och` columns into its 16-column tile.
+            T* const orow = sub == 0 ? out1 : out2;
+            const int64_t orow_off = (static_cast<int64_t>(n) * seq + q) * heads * vd + h * vd;
+            const int och = h * vd - ((h * vd) & ~7);
+            if constexpr (kFused) {
+                if (!block_live) {
+                    // No live row: the block's outputs are zero (rows past T excluded).
+                    if (q < seq)
+                        for (int cpair = 0; 2 * cpair < vd; ++cpair)
+                            *reinterpret_cast<uint32_t*>(orow + orow_off + 2 * cpair) = 0u;
+                    continue;
+                }
+            }
+
             // ---- pass 2: this warp writes keys [kb_w, ke_w) of its 32 rows ----
             const bool all_live = __all_sync(0xffffffffu, row_live);
             const bool use_tmem = block_live && __any_sync(0xffffffffu, row_live) &&
@@ -553,7 +708,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             const int ke_w = min(p_hi * kPiece, seq);
             const int rows_here = min(32, seq - (q0 + qtr * 32));
             const int64_t e_base =
-                (static_cast<int64_t>(n * heads + h) * seq + q0 + qtr * 32) * seq;
+                (static_cast<int64_t>(n * out_heads + h) * seq + q0 + qtr * 32) * seq;
             uint8_t* stage_w = smem + kSmemStage + warp * kStageWarp;
             uint8_t* srow = stage_w + lane * kStageRow;
             auto group_valid = [&](int g) { return g < ngroups && valid[g] != 0u; };
@@ -601,6 +756,21 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 // Next piece's exps are read from TMEM while this one is written out.
                 if (pc + 1 < p_hi && piece_cached(pc + 1))
                     tmem_ld32(tmem + lane_off + kCacheCol + (pc + 1) * (kPiece / 2), c);
+                if constexpr (kFused) {
+                    // The piece's rounded weights go to this sub-slot's P tile (row q_local,
+                    // keys k0..k0+63) once the control warp's previous P.V has read it.
+                    if (p_uses > 0) warp_wait(bar_a_empty + 8 * sub, (p_uses - 1) & 1, abort);
+                    uint8_t* pt = smem + kSmemP + sub * kPTile;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        *reinterpret_cast<uint4*>(pt + sw128_offset(q_local, i)) =
+                            make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar_a_full + 8 * sub);
+                    ++p_uses;
+                    continue;
+                }
                 *reinterpret_cast<uint4*>(srow) = carry;
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
@@ -646,6 +816,36 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 }
                 __syncwarp();
             }
+            if constexpr (kFused) {
+                // O row of this warp's value tensor: accumulator columns of the block's last
+                // score buffer, rounded to T like the attention-value plugin's output.
+                const uint32_t ocol = ((ucount & 1u) ^ 1u) * kChunk + sub * 16;
+                const bool ok = warp_wait(bar_o_full, o_fulls & 1, abort);
+                ++o_fulls;
+                uint32_t r[16];
+                if (ok) {
+                    tc_fence_after();
+                    tmem_ld16(tmem + lane_off + ocol, r);
+                    tmem_wait_ld();
+                    reg_fence(r);
+                    if (q < seq) {
+#pragma unroll
+                        for (int cpair = 0; cpair < 8; ++cpair) {
+                            if (2 * cpair >= vd) break;
+                            // och is 0 or 4 (vd is a multiple of 4).
+                            const float a = __uint_as_float(
+                                och == 0 ? r[2 * cpair] : r[(2 * cpair + 4) & 15]);
+                            const float b2 = __uint_as_float(
+                                och == 0 ? r[2 * cpair + 1] : r[(2 * cpair + 5) & 15]);
+                            *reinterpret_cast<uint32_t*>(orow + orow_off + 2 * cpair) =
+                                pack_pair<T>(a, b2);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_o_free);
+            }
             tc_fence_before();
         }
     }
@@ -659,6 +859,17 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     }
     if (control && kq_pair >= 0) {
         if (!mbar_wait(bar_kq, kq_phase & 1) && lane == 0) atomicExch(&g_zipformer_tc_error, 1u);
+    }
+    if constexpr (kFused) {
+        // P.V MMAs and V loads (the latter only outstanding after an abort).
+        if (control && o_fulls > 0) {
+            if (!mbar_wait(bar_o_full, (o_fulls - 1) & 1) && lane == 0)
+                atomicExch(&g_zipformer_tc_error, 1u);
+        }
+        if (control && v_pending) {
+            if (!mbar_wait(bar_v_full, v_waits & 1) && lane == 0)
+                atomicExch(&g_zipformer_tc_error, 1u);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -703,41 +914,96 @@ int sm_count() {
     return n;
 }
 
+CUtensorMapDataType map_type(int32_t dtype) {
+    return dtype == FGA_HALF ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// Projection map: Q and K rows of one head, 128 rows per box, SWIZZLE_64B.
+bool encode_proj_map(EncodeTiledFn encode, CUtensorMap* map, const void* proj, int32_t dtype,
+                     int batch, int seq, int heads) {
+    const uint64_t pdim = static_cast<uint64_t>(heads) * (2 * kQd + 4);
+    const cuuint64_t dims[3] = {pdim, static_cast<cuuint64_t>(seq), static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {pdim * 2, pdim * 2 * seq};
+    const cuuint32_t box[3] = {kQd, kM, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return encode(map, map_type(dtype), 3, const_cast<void*>(proj), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+// Value map [N, T, H*vd]: boxes of 16 channels x 256 keys, SWIZZLE_32B (MN-major pieces).
+bool encode_value_map(EncodeTiledFn encode, CUtensorMap* map, const void* value, int32_t dtype,
+                      int batch, int seq, int channels) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(seq),
+                                static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(channels) * 2,
+                                   static_cast<cuuint64_t>(channels) * 2 * seq};
+    const cuuint32_t box[3] = {16, kVBox, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return encode(map, map_type(dtype), 3, const_cast<void*>(value), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+template <typename T, bool kFused>
+cudaError_t set_smem_attr() {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(zipformer_weights_tc_kernel<T, kFused>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(SmemEnd<kFused>::bytes));
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    return cudaSuccess;
+}
+
+int next_sched_slot() {
+    static std::atomic<unsigned int> ticket{0};
+    return static_cast<int>(ticket.fetch_add(1u) % kSchedSlots);
+}
+
 template <typename T>
 cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stream) {
     EncodeTiledFn encode = encode_fn();
     if (encode == nullptr) return cudaErrorNotSupported;
-    const CUtensorMapDataType dt = Fmt<T>::v == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    const uint64_t pdim = static_cast<uint64_t>(p.heads) * (2 * kQd + 4);
-    CUtensorMap map;
-    const cuuint64_t dims[3] = {pdim, static_cast<cuuint64_t>(p.length),
-                                static_cast<cuuint64_t>(p.batch)};
-    const cuuint64_t strides[2] = {pdim * sizeof(T), pdim * sizeof(T) * p.length};
-    const cuuint32_t box[3] = {kQd, kM, 1};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    if (encode(&map, dt, 3, const_cast<void*>(p.projection), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
+    CUtensorMap map, unused{};
+    if (!encode_proj_map(encode, &map, p.projection, p.dtype, p.batch, p.length, p.heads))
         return cudaErrorNotSupported;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(zipformer_weights_tc_kernel<T>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBytes));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    if (cudaError_t e = set_smem_attr<T, false>(); e != cudaSuccess) return e;
+    const int out_heads = p.out_heads > 0 ? p.out_heads : p.heads;
+    const int64_t pairs = static_cast<int64_t>(p.batch) * out_heads;
+    const int sms = sm_count();
+    if (sms <= 0) return cudaErrorNotSupported;
+    const int grid = static_cast<int>(pairs < sms ? pairs : sms);
+    zipformer_weights_tc_kernel<T, false><<<grid, kThreads, SmemEnd<false>::bytes, stream>>>(
+        map, unused, unused, static_cast<const T*>(p.projection),
+        static_cast<const T*>(p.position), p.mask, static_cast<T*>(p.weights), nullptr, nullptr,
+        p.length, p.heads, out_heads, 0, static_cast<int>(pairs), next_sched_slot());
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t fused_tc_typed(const ZipformerFusedProblem& p, cudaStream_t stream) {
+    EncodeTiledFn encode = encode_fn();
+    if (encode == nullptr) return cudaErrorNotSupported;
+    const int channels = p.heads * p.value_dim;
+    CUtensorMap map, v1, v2;
+    if (!encode_proj_map(encode, &map, p.projection, p.dtype, p.batch, p.length, p.heads) ||
+        !encode_value_map(encode, &v1, p.value1, p.dtype, p.batch, p.length, channels) ||
+        !encode_value_map(encode, &v2, p.value2, p.dtype, p.batch, p.length, channels))
+        return cudaErrorNotSupported;
+    if (cudaError_t e = set_smem_attr<T, true>(); e != cudaSuccess) return e;
     const int64_t pairs = static_cast<int64_t>(p.batch) * p.heads;
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
     const int grid = static_cast<int>(pairs < sms ? pairs : sms);
-    static std::atomic<unsigned int> ticket{0};
-    const int slot = static_cast<int>(ticket.fetch_add(1u) % kSchedSlots);
-    zipformer_weights_tc_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(
-        map, static_cast<const T*>(p.projection), static_cast<const T*>(p.position), p.mask,
-        static_cast<T*>(p.weights), p.length, p.heads, static_cast<int>(pairs), slot);
+    zipformer_weights_tc_kernel<T, true><<<grid, kThreads, SmemEnd<true>::bytes, stream>>>(
+        map, v1, v2, static_cast<const T*>(p.projection), static_cast<const T*>(p.position),
+        p.mask, nullptr, static_cast<T*>(p.output1), static_cast<T*>(p.output2), p.length,
+        p.heads, p.heads, p.value_dim, static_cast<int>(pairs), next_sched_slot());
     return cudaGetLastError();
 }
 
@@ -757,6 +1023,34 @@ cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem& p, cudaSt
         return cudaErrorNotSupported;
     return p.dtype == FGA_HALF ? weights_tc_typed<__half>(p, stream)
                                : weights_tc_typed<__nv_bfloat16>(p, stream);
+}
+
+cudaError_t launch_zipformer_fused(const ZipformerFusedProblem& p, cudaStream_t stream) {
+    if (p.query_dim != kQd || (p.dtype != FGA_HALF && p.dtype != FGA_BF16))
+        return cudaErrorNotSupported;
+    if (p.length > kMaxT || p.length < 1) return cudaErrorNotSupported;
+    if (static_cast<int64_t>(p.batch) * p.heads > (1ll << 30)) return cudaErrorNotSupported;
+    // One 16-channel V atom per head: vd a multiple of 4 up to 16 puts the head's channels
+    // at offset 0 or 4 of the atom that starts at its first channel rounded down to 8.
+    if (p.value_dim < 4 || p.value_dim > 16 || p.value_dim % 4 != 0) return cudaErrorNotSupported;
+    const int64_t row_bytes = static_cast<int64_t>(p.heads) * (2 * kQd + 4) * 2;
+    const int64_t v_row_bytes = static_cast<int64_t>(p.heads) * p.value_dim * 2;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (row_bytes % 16 != 0 || v_row_bytes % 16 != 0 || !a16(p.projection) || !a16(p.value1) ||
+        !a16(p.value2) || (reinterpret_cast<uintptr_t>(p.output1) & 3u) != 0 ||
+        (reinterpret_cast<uintptr_t>(p.output2) & 3u) != 0 ||
+        (reinterpret_cast<uintptr_t>(p.position) & 7u) != 0 ||
+        (p.weights0 != nullptr && !a16(p.weights0)))
+        return cudaErrorNotSupported;
+    cudaError_t e = p.dtype == FGA_HALF ? fused_tc_typed<__half>(p, stream)
+                                        : fused_tc_typed<__nv_bfloat16>(p, stream);
+    if (e != cudaSuccess || p.weights0 == nullptr) return e;
+    // Head 0's weights for NonlinAttention, by the weights kernel restricted to one head.
+    ZipformerWeightsProblem w{p.projection, p.position, p.mask, p.weights0, p.batch,
+                              p.length, p.heads, p.query_dim, p.dtype};
+    w.out_heads = 1;
+    return p.dtype == FGA_HALF ? weights_tc_typed<__half>(w, stream)
+                               : weights_tc_typed<__nv_bfloat16>(w, stream);
 }
 
 }  // namespace fga

@@ -62,6 +62,7 @@ enum fga_status {
     FGA_ERROR_PRIOR_CUDA_ERROR = 6,
     FGA_ERROR_LAUNCH = 7,
     FGA_ERROR_NO_DEVICE = 8,      /* current device is not sm_100 */
+    FGA_ERROR_UNSUPPORTED = 9,    /* valid, but outside an entry point's stated envelope */
 };
 
 /* Mirrors nvinfer1::PluginTensorDesc minus format (row-major linear is implied). */
@@ -145,6 +146,40 @@ FGA_API size_t fga_zipformer_attention_value_workspace_size(const fga_tensor_des
 FGA_API int32_t fga_zipformer_attention_value_enqueue(const fga_tensor_desc* input_descs,
     const fga_tensor_desc* output_descs, const void* const* inputs, void* const* outputs,
     int32_t num_heads, void* workspace, size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------------
+ * zipformer_attention_fused (weights applied to both SelfAttention values in one pass)
+ *
+ * No reference plugin corresponds to this entry point: it goes beyond the drop-in
+ * surface. It computes what zipformer_relative_attention followed by two
+ * zipformer_attention_value calls (num_heads = H) compute, for the two SelfAttention
+ * modules of a Zipformer layer that share one set of weights
+ * (src/fast_gpu_asr/export/model/zipformer/attention.py:62-73), without writing the
+ * [N, H, T, T] weights: each 64-key piece of rounded weights goes from the softmax
+ * straight into the value MMAs on chip. Head 0's weights, which NonlinAttention reads
+ * (attention.py:130-138), are written as [N, 1, T, T] for a following
+ * fga_zipformer_attention_value_enqueue call with num_heads = 1.
+ *
+ * inputs[0] projection [N, T, H*(2*qd+4)] f16|bf16 (as zipformer_relative_attention)
+ * inputs[1] position   [1, 2T-1, H, 4]     same type
+ * inputs[2] mask       [N, T]              bool, True = padded key
+ * inputs[3] value1     [N, T, H*vd]        same type
+ * inputs[4] value2     [N, T, H*vd]        same type
+ * outputs[0] out1      [N, T, H*vd]        same type
+ * outputs[1] out2      [N, T, H*vd]        same type
+ * outputs[2] weights0  [N, 1, T, T]        same type
+ *
+ * The weights are rounded to the I/O type before they are applied, as the two-plugin
+ * path does; the products are accumulated in fp32. Envelope: f16/bf16, qd = 32, H even,
+ * T <= 768, vd a multiple of 4 in [4, 16], H*vd*2 bytes a multiple of 16, value tensors
+ * and weights0 16-byte aligned, outputs 4-byte aligned. Outside it the entry point
+ * returns FGA_ERROR_UNSUPPORTED and launches nothing. It needs no workspace.
+ * -------------------------------------------------------------------------------- */
+FGA_API int32_t fga_zipformer_attention_fused_check(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs, const fga_tensor_desc* output_descs, int32_t nb_outputs);
+FGA_API int32_t fga_zipformer_attention_fused_enqueue(const fga_tensor_desc* input_descs,
+    const fga_tensor_desc* output_descs, const void* const* inputs, void* const* outputs,
+    void* stream);
 
 /* --------------------------------------------------------------------------------
  * Library identity and diagnostics (no counterpart needed in the reference; the

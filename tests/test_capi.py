@@ -47,7 +47,7 @@ def test_library_exports_every_declared_symbol(library):
 
 
 def test_status_strings(library):
-    for code in range(9):
+    for code in range(10):
         assert library.fga_status_string(code)
     assert library.fga_status_string(0) == b"success"
 
@@ -191,3 +191,80 @@ def test_value_accepts_valid_contract(library):
 ])
 def test_value_rejects_contract_violations(library, att, val, out, heads, status):
     assert value_status(att, val, out, heads) == status
+
+
+# ---- fused Zipformer weights + attention-value (no reference plugin) --------------------
+def fused_descs(n=2, t=65, h=4, qd=32, vd=12, dtype=BF16, **override):
+    d = dict(projection=D(dtype, (n, t, h * (2 * qd + 4))), position=D(dtype, (1, 2 * t - 1, h, 4)),
+             mask=D(BOOL, (n, t)), value1=D(dtype, (n, t, h * vd)), value2=D(dtype, (n, t, h * vd)),
+             out1=D(dtype, (n, t, h * vd)), out2=D(dtype, (n, t, h * vd)),
+             weights0=D(dtype, (n, 1, t, t)))
+    d.update(override)
+    return ([d["projection"], d["position"], d["mask"], d["value1"], d["value2"]],
+            [d["out1"], d["out2"], d["weights0"]])
+
+
+def fused_status(descs):
+    return ops.zipformer_attention_fused_check(*descs)
+
+
+def test_fused_header_declares_its_entry_points():
+    names = declared_symbols()
+    assert {"fga_zipformer_attention_fused_check", "fga_zipformer_attention_fused_enqueue"} <= names
+
+
+def test_fused_accepts_its_envelope(library):
+    for dtype in (F16, BF16):
+        assert fused_status(fused_descs(dtype=dtype)) == 0
+    for h, vd in ((4, 12), (8, 12), (2, 4), (2, 8), (4, 16), (6, 12)):
+        assert fused_status(fused_descs(h=h, vd=vd)) == 0, (h, vd)
+    assert fused_status(fused_descs(n=1, t=1)) == 0
+    assert fused_status(fused_descs(t=768)) == 0
+
+
+@pytest.mark.parametrize("name,kwargs,status", [
+    ("float32", dict(dtype=F32), 9),
+    ("longer-than-768", dict(t=769), 9),
+    ("query-dim-16", dict(qd=16), 9),
+    ("value-dim-6", dict(h=4, vd=6), 9),
+    ("value-dim-20", dict(h=4, vd=20), 9),
+    ("odd-heads", dict(h=3, vd=8), 9),
+])
+def test_fused_rejects_outside_envelope(library, name, kwargs, status):
+    assert fused_status(fused_descs(**kwargs)) == status
+
+
+@pytest.mark.parametrize("name,override,status", [
+    ("mask-length", dict(mask=D(BOOL, (2, 64))), 3),
+    ("position-length", dict(position=D(BF16, (1, 128, 4, 4))), 3),
+    ("value2-shape", dict(value2=D(BF16, (2, 65, 40))), 3),
+    ("value-not-divisible-by-heads", dict(value1=D(BF16, (2, 65, 50)), value2=D(BF16, (2, 65, 50)),
+                                          out1=D(BF16, (2, 65, 50)), out2=D(BF16, (2, 65, 50))), 3),
+    ("out1-length", dict(out1=D(BF16, (2, 64, 48))), 3),
+    ("weights0-heads", dict(weights0=D(BF16, (2, 4, 65, 65))), 3),
+    ("weights0-dtype", dict(weights0=D(F16, (2, 1, 65, 65))), 2),
+    ("value-dtype", dict(value1=D(F16, (2, 65, 48))), 2),
+    ("value-rank", dict(value1=D(BF16, (2, 65, 4, 12))), 2),
+])
+def test_fused_rejects_contract_violations(library, name, override, status):
+    assert fused_status(fused_descs(**override)) == status
+
+
+def test_fused_rejects_wrong_binding_count(library):
+    ins, outs = fused_descs()
+    assert ops.zipformer_attention_fused_check(ins[:4], outs) == 2
+    assert ops.zipformer_attention_fused_check(ins, outs[:2]) == 2
+
+
+def test_fused_enqueue_rejects_null_pointers(library):
+    ins, outs = fused_descs()
+    in_arr, out_arr = _lib.desc_array(ins), _lib.desc_array(outs)
+    ptrs_in = _lib.pointer_array([16] * 4 + [None])
+    ptrs_out = _lib.pointer_array([16] * 3)
+    assert library.fga_zipformer_attention_fused_enqueue(in_arr, out_arr, ptrs_in, ptrs_out,
+                                                         None) == 1
+    ptrs_in = _lib.pointer_array([16] * 5)
+    ptrs_out = _lib.pointer_array([16, None, 16])
+    assert library.fga_zipformer_attention_fused_enqueue(in_arr, out_arr, ptrs_in, ptrs_out,
+                                                         None) == 1
+
