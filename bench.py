@@ -272,7 +272,7 @@ def zipformer_fused_launch_bytes(stacks):
             w0 = n * t * t * 2
             out.append(("zipformer_attention_fused",
                         L.projection.numel() * 2 + L.position.numel() * 2 + L.mask.numel()
-                        + 2 * L.value_a.numel() * 2 + 2 * out_a.numel() * 2 + w0, 2))
+                        + 2 * L.value_a.numel() * 2 + 2 * out_a.numel() * 2 + w0, 1))
             out.append(("zipformer_attention_value",
                         w0 + L.nonlin_value.numel() * 2 + out_nl.numel() * 2, 1))
     return out

@@ -25,14 +25,14 @@ struct ZipformerWeightsProblem {
     const void* projection;  // [N, T, H*(2qd+4)]
     const void* position;    // [1, 2T-1, H, 4]
     const uint8_t* mask;     // [N, T] bool
-    void* weights;           // [N, out_heads, T, T]
+    void* weights;           // [N, H, T, T]
     int32_t batch, length, heads, query_dim;
     int32_t dtype;
-    int32_t out_heads = 0;   // heads [0, out_heads) are computed; 0 means all H
 };
 
 // Zipformer weights applied in the same kernel to the two SelfAttention value tensors
-// (no [N, H, T, T] tensor is written), plus head 0's weights for NonlinAttention.
+// (no [N, H, T, T] tensor is written), plus head 0's weights for NonlinAttention, all
+// in one kernel.
 struct ZipformerFusedProblem {
     const void* projection;  // [N, T, H*(2qd+4)]
     const void* position;    // [1, 2T-1, H, 4]

@@ -334,7 +334,6 @@ cudaError_t launch_parakeet_simt(const ParakeetProblem& p, cudaStream_t s) {
 }
 
 cudaError_t launch_zipformer_weights_simt(const ZipformerWeightsProblem& p, cudaStream_t s) {
-    if (p.out_heads != 0 && p.out_heads != p.heads) return cudaErrorNotSupported;  // all heads only
     switch (p.dtype) {
         case FGA_FLOAT: return zipformer_weights_simt_typed<float>(p, s);
         case FGA_HALF: return zipformer_weights_simt_typed<__half>(p, s);

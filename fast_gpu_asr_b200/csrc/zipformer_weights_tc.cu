@@ -25,6 +25,12 @@
 //           each row's slots are re-aligned from the staging tile with byte permutes; the
 //           partial slots at range ends are written element-wise).
 //
+// Fused variant (kFused, entry point fga_zipformer_attention_fused_enqueue, no reference
+// plugin): pass 2 writes each piece of rounded weights into a P tile and the control
+// warp multiplies it by both value tensors' V pieces (tcgen05, N = 16 each); O1 and O2
+// accumulate in a drained score buffer. The [N, H, T, T] weights are never written, except
+// head 0's ([N, 1, T, T], for NonlinAttention), staged per warp in the band region.
+//
 // Reference semantics (zipformer_relative_attention_plugin.cu:238-327 and 490-566): the
 // content score is stored in T by the reference GEMM (rounded here before the fp32
 // positional add, accumulated in the same order); max over valid keys; exp(x - max);
@@ -207,9 +213,71 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
     return ok;
 }
 
-// kFused = false: attention weights of heads [0, out_heads) written as [N, out_heads, T, T].
-// kFused = true: the weights of every head (out_heads == heads) applied to two value
-// tensors [N, T, heads * vd] (v1_map, v2_map) into out1 and out2; nothing else is written.
+// Fused variant, head 0: one 32-key half (keys k0h..k0h+31) of this warp's 32 rows of the
+// [N, 1, T, T] weights, restricted to [kb_w, ke_w). The halves are staged per warp in
+// the positional-band region (dead during pass 2): 80-byte rows (an odd number of
+// 16-byte chunks, so the row-parallel 16-byte accesses are bank-conflict free) holding
+// the previous 8 keys (carry) and the half, then written as 16-byte stores aligned to
+// the global addresses, as in pass 2 of the weights kernel.
+constexpr int kHalfStageRow = 16 + 32 * 2;
+constexpr int kHalfStageWarp = 32 * kHalfStageRow;
+static_assert(kComputeWarps * kHalfStageWarp + 16 <= 4 * kCopy * 2, "head-0 staging fits the band");
+
+template <typename T>
+__device__ __forceinline__ void store_head0_half(T* __restrict__ out, uint8_t* stage_w,
+                                                 uint4& carry, const uint32_t (&w)[32], int hf,
+                                                 int64_t e_base, int seq, int rows_here,
+                                                 int k0h, int kb_w, int ke_w, bool last) {
+    const int lane = threadIdx.x & 31;
+    uint8_t* srow = stage_w + lane * kHalfStageRow;
+    *reinterpret_cast<uint4*>(srow) = carry;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(srow + 16 + 16 * i) =
+            make_uint4(w[16 * hf + 4 * i], w[16 * hf + 4 * i + 1], w[16 * hf + 4 * i + 2],
+                       w[16 * hf + 4 * i + 3]);
+    carry = make_uint4(w[16 * hf + 12], w[16 * hf + 13], w[16 * hf + 14], w[16 * hf + 15]);
+    __syncwarp();
+    // Staging element i of a row holds key k0h - 8 + i; slot m starts at key k0h - d + 8m.
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const int row = it * 8 + (lane >> 2);
+        const int m = lane & 3;
+        if (row < rows_here) {
+            const int64_t e_row = e_base + static_cast<int64_t>(row) * seq;
+            const int d = static_cast<int>(e_row & 7);
+            const int lo = k0h - d + 8 * m;
+            const uint8_t* sr = stage_w + row * kHalfStageRow;
+            if (lo >= kb_w && lo + 8 <= ke_w) {
+                const int s0 = 8 - d + 8 * m;
+                const uint32_t* wp = reinterpret_cast<const uint32_t*>(sr) + (s0 >> 1);
+                const uint32_t a0 = wp[0], a1 = wp[1], a2 = wp[2], a3 = wp[3], a4 = wp[4];
+                const uint32_t sel = (s0 & 1) ? 0x5432u : 0x3210u;
+                *reinterpret_cast<uint4*>(out + e_row + lo) =
+                    make_uint4(__byte_perm(a0, a1, sel), __byte_perm(a1, a2, sel),
+                               __byte_perm(a2, a3, sel), __byte_perm(a3, a4, sel));
+            } else if (lo + 8 > kb_w && lo < ke_w) {
+                const T* se = reinterpret_cast<const T*>(sr);
+                for (int k = max(lo, kb_w); k < min(lo + 8, ke_w); ++k)
+                    out[e_row + k] = se[k - k0h + 8];
+            }
+        }
+    }
+    if (last && lane < rows_here) {
+        // Keys after the last slot of the range (slot m = 4, always partial).
+        const int64_t e_row = e_base + static_cast<int64_t>(lane) * seq;
+        const int d = static_cast<int>(e_row & 7);
+        const int lo = k0h - d + 32;
+        const T* se = reinterpret_cast<const T*>(srow);
+        for (int k = max(lo, kb_w); k < min(lo + 8, ke_w); ++k) out[e_row + k] = se[k - k0h + 8];
+    }
+    __syncwarp();
+}
+
+// kFused = false: the attention weights, written as [N, H, T, T].
+// kFused = true: the weights of every head applied to two value
+// tensors [N, T, heads * vd] (v1_map, v2_map) into out1 and out2, and, when `out` is not
+// null, head 0's weights written as [N, 1, T, T].
 template <typename T, bool kFused>
 __global__ void __launch_bounds__(kThreads, 1)
 zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
@@ -218,7 +286,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             const T* __restrict__ proj, const T* __restrict__ pos,
                             const uint8_t* __restrict__ mask, T* __restrict__ out,
                             T* __restrict__ out1, T* __restrict__ out2, int seq, int heads,
-                            int out_heads, int vd, int num_pairs, int slot) {
+                            int vd, int num_pairs, int slot) {
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr uint32_t kSmemBar = SmemEnd<kFused>::bar;
     const uint32_t sbase = smem_u32(smem);
@@ -301,7 +369,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     // Control warp: TMA loads of Q and K of every query block of pair p.
     auto load_qk = [&](int p) {
         if (lane == 0) {
-            const int pn = p / out_heads, ph = p - pn * out_heads;
+            const int pn = p / heads, ph = p - pn * heads;
             mbar_expect_tx(bar_kq, 2u * nqb * kM * kRowBytes);
             for (int b = 0; b < nqb; ++b) {
                 tma_load_3d(sbase + kSmemQ + b * kM * kRowBytes, &proj_map, bar_kq, ph * kQd,
@@ -323,8 +391,8 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         // Every thread read slot (iter+1)&1 of the previous pair before this barrier.
         if (tid == 0)
             next_pair[(iter + 1) & 1] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
-        const int n = pair / out_heads;
-        const int h = pair - n * out_heads;
+        const int n = pair / heads;
+        const int h = pair - n * heads;
         const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
         const int buf = iter & 1;
         float* kb = reinterpret_cast<float*>(smem + kSmemKb) + buf * kMaxT;
@@ -688,12 +756,31 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             T* const orow = sub == 0 ? out1 : out2;
             const int64_t orow_off = (static_cast<int64_t>(n) * seq + q) * heads * vd + h * vd;
             const int och = h * vd - ((h * vd) & ~7);
+            const bool write_w0 = kFused && h == 0 && out != nullptr;
+            const int64_t e0_base = (static_cast<int64_t>(n) * seq + q0 + qtr * 32) * seq;
+            uint8_t* const stage_h0 = smem + kSmemBand + warp * kHalfStageWarp;
             if constexpr (kFused) {
                 if (!block_live) {
                     // No live row: the block's outputs are zero (rows past T excluded).
                     if (q < seq)
                         for (int cpair = 0; 2 * cpair < vd; ++cpair)
                             *reinterpret_cast<uint32_t*>(orow + orow_off + 2 * cpair) = 0u;
+                    if (write_w0) {
+                        const int p_lo = sub == 0 ? 0 : split;
+                        const int p_hi = sub == 0 ? split : npieces;
+                        const int rows_here = min(32, seq - (q0 + qtr * 32));
+                        uint32_t zw[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) zw[i] = 0u;
+                        uint4 zc = make_uint4(0u, 0u, 0u, 0u);
+                        for (int pc = p_lo; pc < p_hi; ++pc)
+#pragma unroll
+                            for (int hf = 0; hf < 2; ++hf)
+                                store_head0_half<T>(out, stage_h0, zc, zw, hf, e0_base, seq,
+                                                    rows_here, pc * kPiece + 32 * hf,
+                                                    p_lo * kPiece, min(p_hi * kPiece, seq),
+                                                    pc + 1 == p_hi && hf == 1);
+                    }
                     continue;
                 }
             }
@@ -708,7 +795,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             const int ke_w = min(p_hi * kPiece, seq);
             const int rows_here = min(32, seq - (q0 + qtr * 32));
             const int64_t e_base =
-                (static_cast<int64_t>(n * out_heads + h) * seq + q0 + qtr * 32) * seq;
+                (static_cast<int64_t>(n * heads + h) * seq + q0 + qtr * 32) * seq;
             uint8_t* stage_w = smem + kSmemStage + warp * kStageWarp;
             uint8_t* srow = stage_w + lane * kStageRow;
             auto group_valid = [&](int g) { return g < ngroups && valid[g] != 0u; };
@@ -769,6 +856,14 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     __syncwarp();
                     if (lane == 0) mbar_arrive(bar_a_full + 8 * sub);
                     ++p_uses;
+                    if (write_w0) {
+                        // Head 0's weights of the same piece, for NonlinAttention.
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf)
+                            store_head0_half<T>(out, stage_h0, carry, w, hf, e0_base, seq,
+                                                rows_here, k0 + 32 * hf, kb_w, ke_w,
+                                                pc + 1 == p_hi && hf == 1);
+                    }
                     continue;
                 }
                 *reinterpret_cast<uint4*>(srow) = carry;
@@ -973,15 +1068,14 @@ cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stre
     if (!encode_proj_map(encode, &map, p.projection, p.dtype, p.batch, p.length, p.heads))
         return cudaErrorNotSupported;
     if (cudaError_t e = set_smem_attr<T, false>(); e != cudaSuccess) return e;
-    const int out_heads = p.out_heads > 0 ? p.out_heads : p.heads;
-    const int64_t pairs = static_cast<int64_t>(p.batch) * out_heads;
+    const int64_t pairs = static_cast<int64_t>(p.batch) * p.heads;
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
     const int grid = static_cast<int>(pairs < sms ? pairs : sms);
     zipformer_weights_tc_kernel<T, false><<<grid, kThreads, SmemEnd<false>::bytes, stream>>>(
         map, unused, unused, static_cast<const T*>(p.projection),
         static_cast<const T*>(p.position), p.mask, static_cast<T*>(p.weights), nullptr, nullptr,
-        p.length, p.heads, out_heads, 0, static_cast<int>(pairs), next_sched_slot());
+        p.length, p.heads, 0, static_cast<int>(pairs), next_sched_slot());
     return cudaGetLastError();
 }
 
@@ -1002,8 +1096,9 @@ cudaError_t fused_tc_typed(const ZipformerFusedProblem& p, cudaStream_t stream) 
     const int grid = static_cast<int>(pairs < sms ? pairs : sms);
     zipformer_weights_tc_kernel<T, true><<<grid, kThreads, SmemEnd<true>::bytes, stream>>>(
         map, v1, v2, static_cast<const T*>(p.projection), static_cast<const T*>(p.position),
-        p.mask, nullptr, static_cast<T*>(p.output1), static_cast<T*>(p.output2), p.length,
-        p.heads, p.heads, p.value_dim, static_cast<int>(pairs), next_sched_slot());
+        p.mask, static_cast<T*>(p.weights0), static_cast<T*>(p.output1),
+        static_cast<T*>(p.output2), p.length, p.heads, p.value_dim, static_cast<int>(pairs),
+        next_sched_slot());
     return cudaGetLastError();
 }
 
@@ -1042,15 +1137,8 @@ cudaError_t launch_zipformer_fused(const ZipformerFusedProblem& p, cudaStream_t 
         (reinterpret_cast<uintptr_t>(p.position) & 7u) != 0 ||
         (p.weights0 != nullptr && !a16(p.weights0)))
         return cudaErrorNotSupported;
-    cudaError_t e = p.dtype == FGA_HALF ? fused_tc_typed<__half>(p, stream)
-                                        : fused_tc_typed<__nv_bfloat16>(p, stream);
-    if (e != cudaSuccess || p.weights0 == nullptr) return e;
-    // Head 0's weights for NonlinAttention, by the weights kernel restricted to one head.
-    ZipformerWeightsProblem w{p.projection, p.position, p.mask, p.weights0, p.batch,
-                              p.length, p.heads, p.query_dim, p.dtype};
-    w.out_heads = 1;
-    return p.dtype == FGA_HALF ? weights_tc_typed<__half>(w, stream)
-                               : weights_tc_typed<__nv_bfloat16>(w, stream);
+    return p.dtype == FGA_HALF ? fused_tc_typed<__half>(p, stream)
+                               : fused_tc_typed<__nv_bfloat16>(p, stream);
 }
 
 }  // namespace fga
