@@ -136,3 +136,46 @@ def test_fused_repeated_calls_and_streams():
     for res in outs:
         for a, b in zip(res, first):
             np.testing.assert_array_equal(a.float().cpu().numpy(), b)
+
+
+def test_fused_guard_bands_and_graph_replay():
+    """Outputs inside larger buffers (guard bands untouched), odd T (rows of head 0's
+    weights start at 2-byte offsets), and CUDA-graph replay of the call."""
+    x = cases.zipformer_inputs(3, 187, lengths=[187, 90, 5])
+    v1, v2 = values_for(x, 12, 11)
+    proj, pos, mask, g1, g2 = to_gpu(x, v1, v2, "bfloat16")
+    n, t = proj.shape[:2]
+    dt = proj.dtype
+
+    def guarded(shape, align):
+        count = int(np.prod(shape))
+        store = torch.full((count + 2 * align,), 7, dtype=dt, device="cuda")
+        return store, store[align : align + count].view(shape)
+
+    s1, o1 = guarded(g1.shape, 256)
+    s2, o2 = guarded(g2.shape, 256)
+    s0, w0 = guarded((n, 1, t, t), 256)
+    torch.cuda.synchronize()
+    zipformer_attention_fused(proj, pos, mask, g1, g2, out1=o1, out2=o2, weights0=w0)
+    torch.cuda.synchronize()
+    for store in (s1, s2, s0):
+        assert (store[:256] == 7).all() and (store[-256:] == 7).all()
+    first = [a.float().cpu().numpy() for a in (o1, o2, w0)]
+    w = oracle_weights(x["projection"], x["position"], x["mask"], "bfloat16")
+    np.testing.assert_allclose(first[0], oracle_value(w, v1, 4, "bfloat16"), rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(first[2], w[:, :1], rtol=cases.WEIGHT_RTOL["bfloat16"],
+                               atol=cases.WEIGHT_ATOL["bfloat16"])
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        zipformer_attention_fused(proj, pos, mask, g1, g2, out1=o1, out2=o2, weights0=w0,
+                                  stream=stream)
+    for _ in range(2):
+        for a in (o1, o2, w0):
+            a.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        for a, b in zip((o1, o2, w0), first):
+            np.testing.assert_array_equal(a.float().cpu().numpy(), b)
+    for store in (s1, s2, s0):
+        assert (store[:256] == 7).all() and (store[-256:] == 7).all()
