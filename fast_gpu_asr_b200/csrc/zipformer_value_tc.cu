@@ -108,11 +108,13 @@ __host__ __device__ constexpr Layout make_layout(int cpad, int seq) {
     l.vatom = static_cast<uint32_t>(kKc) * l.vw * 2u;
     l.vstage = (static_cast<uint32_t>(cpad) / l.vw) * l.vatom;
     const bool narrow = cpad <= 128;
-    l.sup = narrow ? 3u : 1u;
+    const uint32_t nchunks = static_cast<uint32_t>((seq + kKc - 1) / kKc);
+    // A super-chunk never spans more chunks than the row has (short rows would otherwise
+    // fill boxes that are mostly past the row's end).
+    l.sup = narrow ? (nchunks < 3u ? nchunks : 3u) : 1u;
     l.raw_row = raw_row_bytes(static_cast<int>(l.sup));
     l.raw_stage = raw_stage_bytes(static_cast<int>(l.sup));
     l.raw_stages = narrow ? 3u : 4u;
-    const uint32_t nchunks = static_cast<uint32_t>((seq + kKc - 1) / kKc);
     for (l.a_tiles = 3; l.a_tiles >= 2 && l.vres == 0; --l.a_tiles) {
         const uint32_t fixed = l.raw_stages * l.raw_stage + l.a_tiles * kATile + 1024 + kBarBytes;
         if (nchunks <= kMaxVRes && fixed + nchunks * l.vstage <= kSmemLimit) {
