@@ -2,13 +2,15 @@
  * fga_attention.h - C ABI of the B200 (sm_100a) encoder self-attention library
  * (libfga_attention.so).
  *
- * The three entry points below replace the bodies of the `enqueue` methods of the
- * reference's three attention TensorRT plugins. Each takes the same tensor
+ * The first three entry points below replace the bodies of the `enqueue` methods of
+ * the reference's three attention TensorRT plugins. Each takes the same tensor
  * descriptors (type, rank, dims), the same raw device pointers in the same binding
  * order and the same stream, and returns 0 on success and nonzero on failure, so a
  * TensorRT shim converts `PluginTensorDesc` to `fga_tensor_desc` one field at a time
  * and forwards. No torch, TensorRT or CUDA type appears in any signature: a stream is
- * passed as `void*` (a `cudaStream_t`), device buffers as `void*`.
+ * passed as `void*` (a `cudaStream_t`), device buffers as `void*`. A fourth entry
+ * point, fga_zipformer_attention_fused_enqueue, has no reference plugin (it replaces
+ * three plugin calls of one Zipformer layer at once) and follows the same conventions.
  *
  * Memory: the caller owns every input, output and workspace buffer; no entry point
  * allocates device memory, and none needs workspace (the `*_workspace_size` queries
