@@ -11,6 +11,8 @@ bit-identical to the weights entry point's head 0 (the same kernel computes them
 
 from __future__ import annotations
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -179,3 +181,27 @@ def test_fused_guard_bands_and_graph_replay():
             np.testing.assert_array_equal(a.float().cpu().numpy(), b)
     for store in (s1, s2, s0):
         assert (store[:256] == 7).all() and (store[-256:] == 7).all()
+
+
+FUSED_GOLDEN = [p for p in sorted(
+    (Path(__file__).parent / "golden").glob("zipformer_*.npz")) if "fp32" not in p.stem]
+
+
+@pytest.mark.parametrize("path", FUSED_GOLDEN, ids=lambda p: p.stem)
+def test_fused_matches_reference_golden_vectors(path):
+    """Fixtures generated from the reference's own modules (tests/golden/make_golden.py):
+    both SelfAttention outputs, head 0's weights, and NonlinAttention applied to them.
+    The outputs compose two operators, so they get the f16/bf16 output bound (2e-2)."""
+    g = np.load(path)
+    dt = str(g["dtype"])
+    x = dict(projection=g["projection"], position=g["position"], mask=g["mask"])
+    o1, o2, w0 = fused_on_gpu(x, g["value_a"], g["value_b"], dt)
+    np.testing.assert_allclose(o1, g["out_a"], rtol=2e-2, atol=2e-2)
+    np.testing.assert_allclose(o2, g["out_b"], rtol=2e-2, atol=2e-2)
+    np.testing.assert_allclose(w0, g["weights"][:, :1], rtol=cases.WEIGHT_RTOL[dt],
+                               atol=cases.WEIGHT_ATOL[dt])
+    tdt = getattr(torch, dt)
+    nl = zipformer_attention_value(torch.from_numpy(w0).to("cuda", tdt),
+                                   torch.from_numpy(g["nonlin_value"]).to("cuda", tdt), 1)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(nl.float().cpu().numpy(), g["nonlin_out"], rtol=2e-2, atol=2e-2)
