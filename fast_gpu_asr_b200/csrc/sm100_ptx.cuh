@@ -94,7 +94,7 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         : "memory");
 }
 
-// Packed fp32 pairs: sm_100 executes add/mul/fma on two fp32 lanes per instruction, with
+// Packed fp32 pairs: sm_100 executes add/fma on two fp32 lanes per instruction, with
 // the rounding of the scalar forms (round to nearest even, subnormals kept).
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
     uint64_t r;
@@ -109,11 +109,6 @@ __device__ __forceinline__ float2 f2_unpack(uint64_t v) {
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     uint64_t r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
 __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
