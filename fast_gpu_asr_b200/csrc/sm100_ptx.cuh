@@ -116,6 +116,14 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
+// 2^x on the MUFU unit (ex2.approx with flush-to-zero; relative error about 2^-22;
+// -inf gives 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Three-input fp32 maximum (same NaN and signed-zero rules as fmaxf).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float r;

@@ -130,18 +130,6 @@ template <typename T> struct Fmt;
 template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
 template <> struct Fmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
 
-__device__ __forceinline__ float fast_exp2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-__device__ __forceinline__ float max3(float a, float b, float c) {
-    float d;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
-
 // a0 += q * lo(w), a1 += q * hi(w): T x T products accumulated in fp32 (exact products,
 // the same arithmetic as converting both operands to fp32 first).
 template <typename T> __device__ __forceinline__ void fma_pair(float& a0, float& a1, uint16_t q,
@@ -709,9 +697,9 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             s[4 * t + 3] = fminf(s[4 * t + 3], m4.w);
                         }
                     }
-                    float gm = max3(s[0], s[1], s[2]);
+                    float gm = fmax3(s[0], s[1], s[2]);
 #pragma unroll
-                    for (int e = 3; e < 31; e += 2) gm = max3(gm, s[e], s[e + 1]);
+                    for (int e = 3; e < 31; e += 2) gm = fmax3(gm, s[e], s[e + 1]);
                     gm = fmaxf(gm, s[31]);
                     const float m_new = fmaxf(m_run, gm);
                     const float mb = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
