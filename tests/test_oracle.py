@@ -124,3 +124,20 @@ def test_oracle_value_nonlinear_uses_head_zero():
     out = zipformer_attention_value(a, v, 1)
     assert np.isfinite(out).all()
     np.testing.assert_allclose(out, np.einsum("nqk,nkc->nqc", a[:, 0], v), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("path", [p for p in GOLDEN if p.stem.startswith("zipformer")],
+                         ids=lambda p: p.stem)
+def test_oracle_composition_matches_reference_layer_outputs(path):
+    """The oracle of the fused Zipformer entry point: the oracle's own weights applied to
+    the three value tensors (not the fixture's weights) reproduce the reference layer's
+    outputs within the f16/bf16 output bound (fp32: 1e-5)."""
+    g = np.load(path)
+    dt = str(g["dtype"])
+    w = zipformer_relative_attention(g["projection"], g["position"], g["mask"], dt)
+    heads = int(g["num_heads"])
+    tol = 1e-5 if dt == "float32" else 2e-2
+    for value, out, vh in (("value_a", "out_a", heads), ("value_b", "out_b", heads),
+                           ("nonlin_value", "nonlin_out", 1)):
+        got = zipformer_attention_value(w, g[value], vh, dt)
+        np.testing.assert_allclose(got, g[out], rtol=tol, atol=tol)
