@@ -57,6 +57,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-secondary", action="store_true",
+                   help="default workload only: leave out the zipformer, parakeet_long and "
+                        "zipformer_fused sub-lines")
     args = p.parse_args()
     if args.batch is None:
         args.batch = 16 if args.workload == "parakeet_long" else 256
@@ -550,20 +553,34 @@ def ragged_arm(args, world, rank, local):
 
 
 # ---- our arm ---------------------------------------------------------------------------------
-def ours_arm(args, world, rank, local):
+def device_bus_id(local: int):
+    import torch
+
+    props = torch.cuda.get_device_properties(local)
+    bus = getattr(props, "pci_bus_id", None)
+    if bus is None:
+        return None
+    return (f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:"
+            f"{getattr(props, 'pci_device_id', 0):02x}.0")
+
+
+def sub_args(args, workload: str):
+    """The arguments of a secondary workload of the default line (its own default batch)."""
+    a = argparse.Namespace(**vars(args))
+    a.workload = workload
+    a.batch = 16 if workload == "parakeet_long" else 256
+    return a
+
+
+def measure_workload(args, world, rank, local, peaks, *, with_e2e=True, with_cpu=True,
+                     with_gpu_reference=False) -> dict:
+    """Build one workload, run W warm-up and K timed steps (CUDA events around every launch
+    on the launching stream, max over ranks), and return its line fields."""
     import torch
 
     from fast_gpu_asr_b200 import _lib
 
-    _lib.library()
-    peaks = load_peaks()
     stream = torch.cuda.Stream()
-    dev_props = torch.cuda.get_device_properties(local)
-    bus = getattr(dev_props, "pci_bus_id", None)
-    bus_id = None
-    if bus is not None:
-        bus_id = f"{getattr(dev_props, 'pci_domain_id', 0):08x}:{bus:02x}:{getattr(dev_props, 'pci_device_id', 0):02x}.0"
-
     if is_parakeet(args):
         layers, outs, audio, flops, nbytes = build_parakeet(args, rank)
         launch_kinds = [("parakeet_relative_attention", nbytes)] * len(layers)
@@ -574,7 +591,6 @@ def ours_arm(args, world, rank, local):
         stacks, audio, _ = build_zipformer(args, rank, fused=True)
         calls = zipformer_fused_launch_bytes(stacks)
         launch_kinds = [(name, nb) for name, nb, _ in calls]
-        kernels_per_step = sum(k for _, _, k in calls)
         total_bytes = float(sum(nb for _, nb in launch_kinds))
 
         def step(events=None):
@@ -586,8 +602,6 @@ def ours_arm(args, world, rank, local):
         def step(events=None):
             run_zipformer_step(stacks, stream, events)
     n_launch = len(launch_kinds)
-    if args.workload != "zipformer_fused":
-        kernels_per_step = n_launch
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -599,7 +613,7 @@ def ours_arm(args, world, rank, local):
     events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
                for _ in range(n_launch)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(bus_id) if rank == 0 else None
+    sampler = ClockSampler(device_bus_id(local)) if rank == 0 else None
     barrier(world)
     torch.cuda.synchronize()
     if sampler:
@@ -663,10 +677,19 @@ def ours_arm(args, world, rank, local):
                     "step_hbm_frac": total_bytes / (ms_per_step / 1000.0) / 1e9
                     / peaks["hbm_gbs"],
                     "variant": variant}
-    gpu_launches = args.steps * kernels_per_step
+    # One kernel per entry point call (the weights and fused calls also queue a 4-byte
+    # memset of their work counter, which is not a kernel of this library).
+    gpu_launches = args.steps * n_launch
+
+    gpu_ref = None
+    if with_gpu_reference:
+        if is_parakeet(args):
+            gpu_ref = gpu_reference_parakeet(layers, args, world, peaks, ms_per_step)
+        else:
+            gpu_ref = gpu_reference_zipformer(stacks, audio, world, peaks, ms_per_step)
 
     e2e = None
-    if not args.no_e2e:
+    if with_e2e and not args.no_e2e:
         if is_parakeet(args):
             e2e = e2e_parakeet(args, layers, audio, world)
         else:
@@ -674,19 +697,183 @@ def ours_arm(args, world, rank, local):
                                 fused=args.workload == "zipformer_fused")
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if with_cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_leg(args)(args.cpu_seconds)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
+    return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": workload_config(args)["dtype"], "data": "synthetic",
+            "config": workload_config(args), "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": e2e, "gpu_reference": gpu_ref, "gpu_launches": gpu_launches,
+            "clocks": clocks, "audio_seconds_per_step_per_gpu": audio}
+
+
+# Secondary workloads carried in the default line (same K and W, each its own timed region).
+SECONDARY = ("zipformer", "parakeet_long", "zipformer_fused")
+
+
+def ours_arm(args, world, rank, local):
+    import torch
+
+    from fast_gpu_asr_b200 import _lib
+
+    _lib.library()
+    peaks = load_peaks()
+    line = measure_workload(args, world, rank, local, peaks,
+                            with_gpu_reference=args.workload in ("parakeet", "zipformer"))
+    if args.workload == "parakeet" and not args.no_secondary:
+        for name in SECONDARY:
+            torch.cuda.empty_cache()
+            sub = measure_workload(sub_args(args, name), world, rank, local, peaks,
+                                   with_e2e=name != "zipformer_fused",
+                                   with_cpu=name != "zipformer_fused",
+                                   with_gpu_reference=name == "zipformer")
+            line[name] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "dtype", "config",
+                                              "roofline", "e2e", "cpu_baseline",
+                                              "gpu_reference", "gpu_launches", "clocks")}
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": workload_config(args)["dtype"], "data": "synthetic",
-                "config": workload_config(args), "roofline": roofline, "cpu_baseline": cpu,
-                "e2e": e2e, "gpu_launches": gpu_launches, "clocks": clocks,
-                "audio_seconds_per_step_per_gpu": audio}
         print(json.dumps(line), flush=True)
+
+
+# ---- the reference pipeline on this GPU ------------------------------------------------------
+def _time_ms(fn, stream, reps: int) -> float:
+    import torch
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        fn()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(reps):
+            fn()
+        end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / reps
+
+
+def gpu_reference_parakeet(layers, args, world, peaks, our_ms_per_step):
+    """The reference plugin's pipeline restated on this B200 (TensorRT and the plugin
+    sources cannot run here): per layer and head, the three cuBLAS GEMMs it issues
+    (``parakeet_relative_attention_plugin.cu:1052-1133``: (Q+u)K^T and (Q+v)P^T into HBM
+    score buffers, then weights x V) timed with CUDA events through torch.matmul, plus its
+    softmax pass (``:452-538``: reads both score buffers, writes the weights) and bias pass
+    (``:268-281``) counted at the measured HBM copy rate, i.e. at their floor. The sum is a
+    lower bound on the reference pipeline's time on this GPU. ``torch_eager_ms`` also times
+    the whole pipeline in unfused torch ops (an upper bound)."""
+    import torch
+
+    L = layers[0]
+    n, t, c3 = L.qkv.shape
+    c, heads, d = c3 // 3, 8, 128
+    dt = L.qkv.dtype
+    qkv = L.qkv.view(n, t, 3, heads, d)
+    q = [qkv[:, :, 0, h].contiguous() for h in range(heads)]     # [N, T, D]
+    k = [qkv[:, :, 1, h].contiguous() for h in range(heads)]
+    v = [qkv[:, :, 2, h].contiguous() for h in range(heads)]
+    p = [L.position[0, :, h * d:(h + 1) * d].contiguous() for h in range(heads)]  # [2T-1, D]
+    scores = torch.empty((n, t, t), dtype=dt, device="cuda")
+    pos_scores = torch.empty((n, t, 2 * t - 1), dtype=dt, device="cuda")
+    out = torch.empty((n, t, d), dtype=dt, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def gemms():
+        for h in range(heads):
+            torch.matmul(q[h], k[h].transpose(1, 2), out=scores)
+            torch.matmul(q[h], p[h].t(), out=pos_scores)
+            torch.matmul(scores, v[h], out=out)
+
+    gemm_ms = _time_ms(gemms, stream, 3)
+    elem = 2
+    softmax_bytes = heads * n * t * t * elem * 3            # read two score rows, write weights
+    bias_bytes = 3 * n * t * c * elem                        # read Q, write Q+u and Q+v
+    floor_ms = (softmax_bytes + bias_bytes) / (peaks["hbm_gbs"] * 1e9) * 1e3
+    layer_ms = gemm_ms + floor_ms
+    lengths = L.valid_lengths.long()
+
+    def eager():
+        qf = L.qkv.view(n, t, 3, heads, d).permute(2, 0, 3, 1, 4)
+        qu = (qf[0].float() + L.content_bias.float()[None, :, None, :]).to(dt)
+        qv = (qf[0].float() + L.position_bias.float()[None, :, None, :]).to(dt)
+        pp = L.position[0].view(2 * t - 1, heads, d).permute(1, 0, 2)
+        sc = torch.matmul(qu, qf[1].transpose(-1, -2))
+        ps = torch.matmul(qv, pp.transpose(-1, -2))
+        shifted = ps.as_strided((n, heads, t, t), (ps.stride(0), ps.stride(1), 2 * t - 2, 1),
+                                ps.storage_offset() + t - 1)
+        logits = (sc.float() + shifted.float()) * L.scale
+        mask = torch.arange(t, device="cuda")[None, :] >= lengths[:, None]
+        logits.masked_fill_(mask[:, None, None, :], float("-inf"))
+        w = torch.softmax(logits, dim=-1).nan_to_num_(0.0).to(dt)
+        return torch.matmul(w, qf[2])
+
+    eager_ms = _time_ms(eager, stream, 2)
+    nlayers = len(layers)
+    ref_step_ms = allreduce_max(layer_ms * nlayers, world)
+    audio = wl_audio_parakeet(L)
+    return {"value": audio * world / (ref_step_ms / 1000.0), "unit": UNIT,
+            "ms_per_step": ref_step_ms,
+            "what": "reference plugin pipeline on this GPU: its cuBLAS GEMMs (timed) + its "
+                    "softmax and bias passes at the measured HBM copy rate (a lower bound)",
+            "gemm_ms_per_layer": gemm_ms, "softmax_floor_ms_per_layer": floor_ms,
+            "torch_eager_ms_per_layer": eager_ms,
+            "speedup_of_ours": ref_step_ms / our_ms_per_step}
+
+
+def wl_audio_parakeet(layer) -> float:
+    from fast_gpu_asr_b200 import workloads as wl
+
+    return wl.parakeet_audio_seconds(layer.valid_lengths)
+
+
+def gpu_reference_zipformer(stacks, audio, world, peaks, our_ms_per_step):
+    """The reference plugins' pipeline restated on this B200, per layer: the weights plugin's
+    per-head cuBLAS GEMM writing the content scores into the [N, H, T, T] output
+    (``zipformer_relative_attention_plugin.cu:490-566``) and the three attention-value
+    calls (``zipformer_attention_value_plugin.cu:438-572``, cuBLAS GEMMs here) timed with CUDA
+    events through torch.matmul, plus the weights plugin's in-place softmax pass (reads the
+    scores and positional queries, writes the weights) counted at the measured HBM copy
+    rate. The sum is a lower bound on the reference pipeline's time on this GPU."""
+    import torch
+
+    stream = torch.cuda.Stream()
+    total_ms = 0.0
+    per_stack = []
+    for heads, weights, layers, (out_self, out_nl, *_) in stacks:
+        L = layers[0]
+        n, t = L.projection.shape[:2]
+        dt = L.projection.dtype
+        proj = L.projection.view(n, t, heads, 68)
+        q = [proj[:, :, h, :32].contiguous() for h in range(heads)]
+        k = [proj[:, :, h, 32:64].contiguous() for h in range(heads)]
+        scores = torch.empty((n, t, t), dtype=dt, device="cuda")
+        w = weights.view(n, heads, t, t)
+        va = L.value_a.view(n, t, heads, 12).permute(0, 2, 1, 3).contiguous()
+        vb = L.value_b.view(n, t, heads, 12).permute(0, 2, 1, 3).contiguous()
+        vn = L.nonlin_value
+        oa = torch.empty_like(va)
+        on = torch.empty_like(vn)
+
+        def gemms():
+            for h in range(heads):
+                torch.matmul(q[h], k[h].transpose(1, 2), out=scores)
+            torch.matmul(w, va, out=oa)
+            torch.matmul(w, vb, out=oa)
+            torch.matmul(w[:, 0], vn, out=on)
+
+        gemm_ms = _time_ms(gemms, stream, 3)
+        softmax_bytes = n * heads * t * t * 2 * 2 + n * t * heads * 8
+        floor_ms = softmax_bytes / (peaks["hbm_gbs"] * 1e9) * 1e3
+        per_stack.append({"T": t, "gemm_ms": gemm_ms, "softmax_floor_ms": floor_ms,
+                          "layers": len(layers)})
+        total_ms += (gemm_ms + floor_ms) * len(layers)
+    ref_step_ms = allreduce_max(total_ms, world)
+    return {"value": audio * world / (ref_step_ms / 1000.0), "unit": UNIT,
+            "ms_per_step": ref_step_ms,
+            "what": "reference plugins' pipeline on this GPU: content-score GEMMs and the "
+                    "attention-value GEMMs (timed) + the softmax pass at the measured HBM "
+                    "copy rate (a lower bound)",
+            "per_stack": per_stack, "speedup_of_ours": ref_step_ms / our_ms_per_step}
 
 
 def _pipelined(nlayers_total, h2d, compute, d2h):

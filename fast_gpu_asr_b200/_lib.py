@@ -12,7 +12,8 @@ from pathlib import Path
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "libfga_attention.so"
 FGA_MAX_DIMS = 8
-ABI_VERSION = 1
+ABI_VERSION = 2
+SCHED_WORKSPACE_BYTES = 256  # FGA_SCHED_WORKSPACE_BYTES
 
 # enum fga_data_type (== nvinfer1::DataType numbering)
 FGA_FLOAT = 0
@@ -32,6 +33,8 @@ STATUS_NAMES = {
     7: "FGA_ERROR_LAUNCH",
     8: "FGA_ERROR_NO_DEVICE",
     9: "FGA_ERROR_UNSUPPORTED",
+    10: "FGA_ERROR_WORKSPACE",
+    11: "FGA_ERROR_DEVICE_ABORT",
 }
 
 
@@ -84,11 +87,15 @@ SYMBOLS = {
          ctypes.c_size_t, _VP)),
     "fga_zipformer_attention_fused_check": (
         ctypes.c_int32, (_P, ctypes.c_int32, _P, ctypes.c_int32)),
+    "fga_zipformer_attention_fused_workspace_size": (ctypes.c_size_t, (_P, ctypes.c_int32)),
     "fga_zipformer_attention_fused_enqueue": (
-        ctypes.c_int32, (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP)),
+        ctypes.c_int32,
+        (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP, ctypes.c_size_t, _VP)),
     "fga_abi_version": (ctypes.c_int32, ()),
     "fga_status_string": (ctypes.c_char_p, (ctypes.c_int32,)),
     "fga_last_kernel_variant": (ctypes.c_char_p, ()),
+    "fga_device_status": (ctypes.c_int32, (_VP, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32))),
+    "fga_debug_set_wait_limit_ns": (None, (ctypes.c_uint64,)),
 }
 
 

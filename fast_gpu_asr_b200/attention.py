@@ -66,6 +66,46 @@ def _check(status: int, op: str) -> None:
         raise _lib.AttentionError(status, op)
 
 
+def _torch_stream(stream):
+    if stream is None:
+        return torch.cuda.current_stream()
+    if isinstance(stream, torch.cuda.Stream):
+        return stream
+    return torch.cuda.ExternalStream(int(stream))
+
+
+def _workspace(nbytes: int, device, workspace: torch.Tensor | None, stream):
+    """(pointer, size) of the call's workspace: the caller's tensor, or a fresh one from
+    torch's caching allocator on the launch stream (stream-ordered reuse, so no two
+    launches in flight share one)."""
+    if nbytes == 0:
+        return None, 0
+    if workspace is None:
+        with torch.cuda.stream(_torch_stream(stream)):
+            workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    if not workspace.is_cuda or not workspace.is_contiguous():
+        raise ValueError("workspace must be a contiguous CUDA tensor")
+    return workspace.data_ptr(), workspace.numel() * workspace.element_size()
+
+
+def device_status(stream=None, clear: bool = True) -> tuple[int, int]:
+    """``(status, detail)`` of ``fga_device_status`` on the current device: waits for the
+    work queued on ``stream``; status 0 when no kernel gave up a bounded wait since the last
+    clear, 11 (FGA_ERROR_DEVICE_ABORT) when one did; ``detail`` holds the error words."""
+    import ctypes
+
+    detail = ctypes.c_uint32(0)
+    status = _lib.library().fga_device_status(_stream_handle(stream), int(clear),
+                                              ctypes.byref(detail))
+    return int(status), int(detail.value)
+
+
+def set_wait_limit_ns(limit_ns: int) -> None:
+    """Test hook: bounded-wait limit of the Zipformer weights and fused kernels for later
+    launches from this thread (0 restores the default of 2 s)."""
+    _lib.library().fga_debug_set_wait_limit_ns(int(limit_ns))
+
+
 # ---- shape checks (no device needed) -----------------------------------------------
 def parakeet_relative_attention_check(input_descs, output_desc, scale: float) -> int:
     lib = _lib.library()
@@ -113,8 +153,12 @@ def parakeet_relative_attention(qkv: torch.Tensor, position: torch.Tensor,
 
 def zipformer_relative_attention(projection: torch.Tensor, position: torch.Tensor,
                                  mask: torch.Tensor, *, out: torch.Tensor | None = None,
-                                 stream=None) -> torch.Tensor:
-    """Normalised relative-attention weights ``[N, H, T, T]``."""
+                                 stream=None, workspace: torch.Tensor | None = None
+                                 ) -> torch.Tensor:
+    """Normalised relative-attention weights ``[N, H, T, T]``.
+
+    ``workspace`` (optional): at least ``FGA_SCHED_WORKSPACE_BYTES`` of device memory for
+    the launch's work counter; by default a fresh one per call."""
     lib = _lib.library()
     if out is None:
         n, t = projection.shape[0], projection.shape[1]
@@ -126,8 +170,10 @@ def zipformer_relative_attention(projection: torch.Tensor, position: torch.Tenso
     outs = _lib.desc_array([_desc(out)])
     in_ptrs = _lib.pointer_array([_ptr(x, nm) for x, nm in zip(tensors, names)])
     out_ptrs = _lib.pointer_array([_ptr(out, "weights")])
+    ws, ws_bytes = _workspace(lib.fga_zipformer_relative_attention_workspace_size(ins, 3),
+                              projection.device, workspace, stream)
     status = lib.fga_zipformer_relative_attention_enqueue(
-        ins, outs, in_ptrs, out_ptrs, None, 0, _stream_handle(stream))
+        ins, outs, in_ptrs, out_ptrs, ws, ws_bytes, _stream_handle(stream))
     _check(status, "zipformer_relative_attention")
     return out
 
@@ -159,7 +205,8 @@ def zipformer_attention_fused_check(input_descs, output_descs) -> int:
 def zipformer_attention_fused(projection: torch.Tensor, position: torch.Tensor,
                               mask: torch.Tensor, value1: torch.Tensor, value2: torch.Tensor, *,
                               out1: torch.Tensor | None = None, out2: torch.Tensor | None = None,
-                              weights0: torch.Tensor | None = None, stream=None):
+                              weights0: torch.Tensor | None = None, stream=None,
+                              workspace: torch.Tensor | None = None):
     """``(out1, out2, weights0)``: ``zipformer_attention_value(W, value_i, H)`` for the
     weights ``W = zipformer_relative_attention(projection, position, mask)``, and
     ``W[:, :1]``, without materialising ``W``.
@@ -184,7 +231,9 @@ def zipformer_attention_fused(projection: torch.Tensor, position: torch.Tensor,
     in_ptrs = _lib.pointer_array([_ptr(x, nm) for x, nm in zip(tensors, names)])
     out_ptrs = _lib.pointer_array(
         [_ptr(x, nm) for x, nm in zip(outputs, ("out1", "out2", "weights0"))])
+    ws, ws_bytes = _workspace(lib.fga_zipformer_attention_fused_workspace_size(ins, 5),
+                              projection.device, workspace, stream)
     status = lib.fga_zipformer_attention_fused_enqueue(
-        ins, outs, in_ptrs, out_ptrs, _stream_handle(stream))
+        ins, outs, in_ptrs, out_ptrs, ws, ws_bytes, _stream_handle(stream))
     _check(status, "zipformer_attention_fused")
     return out1, out2, weights0

@@ -9,10 +9,14 @@ static CUDA runtime. The library is written to a temporary name and renamed into
 place only after the link succeeds. Nothing is rebuilt when the library is newer than
 every source and header.
 
-When TensorRT headers are found (``NvInfer.h`` under ``$TENSORRT_ROOT/include`` or the
-CUDA include directory), the three TensorRT plugin shims in ``csrc/trt/`` are built as
-well, one shared object per plugin as in the reference
-(``src/fast_gpu_asr/tensorrt_plugins/build.py``).
+When TensorRT's headers are found (``NvInfer.h`` under ``$TENSORRT_ROOT/include``, the
+CUDA include directory or ``/usr/include/x86_64-linux-gnu``), the three TensorRT plugin
+shims in ``csrc/trt/`` are built as well, one shared object per plugin with the
+reference's library names (``src/fast_gpu_asr/tensorrt_plugins/constants.py:45-67``),
+each linked against ``libfga_attention.so`` and loaded by
+``fast_gpu_asr_b200.tensorrt_plugins.load_tensorrt_plugins``. This image has no TensorRT;
+the shims' contracts are compiled and tested on CPU against a stub header
+(``tests/test_trt_shims.py``).
 """
 
 from __future__ import annotations
@@ -92,7 +96,54 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
     tmp.replace(LIBRARY)
+    trt_include = tensorrt_include()
+    if trt_include is not None:
+        lib_dir = trt_include.parent / "lib"
+        link = (f"-L{lib_dir}",) if lib_dir.is_dir() else ()
+        build_trt_shims(trt_include, extra=(*link, "-lnvinfer"))
     return LIBRARY
+
+
+TRT_DIR = CSRC / "trt"
+TRT_SHIMS = (
+    "parakeet_relative_attention_plugin",
+    "zipformer_relative_attention_plugin",
+    "zipformer_attention_value_plugin",
+)
+
+
+def tensorrt_include() -> Path | None:
+    """Directory holding TensorRT's ``NvInfer.h``, or None."""
+    candidates = []
+    if os.environ.get("TENSORRT_ROOT"):
+        candidates.append(Path(os.environ["TENSORRT_ROOT"]) / "include")
+    candidates += [Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include",
+                   Path("/usr/include/x86_64-linux-gnu"), Path("/usr/include")]
+    for c in candidates:
+        if (c / "NvInfer.h").is_file():
+            return c
+    return None
+
+
+def build_trt_shims(include_dir: Path, out_dir: Path = PACKAGE_DIR, rpath: str = "$ORIGIN",
+                    extra: tuple[str, ...] = ()) -> list[Path]:
+    """Compile each TensorRT plugin shim into ``out_dir/<name>.so`` (host C++ only), linked
+    against ``libfga_attention.so`` (found through ``rpath``)."""
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("a C++ compiler is required for the TensorRT plugin shims")
+    cuda_include = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+    out_dir.mkdir(parents=True, exist_ok=True)
+    built = []
+    for name in TRT_SHIMS:
+        target = out_dir / f"{name}.so"
+        cmd = [cxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-fvisibility=hidden", "-Wall",
+               "-Wextra", "-Werror", "-I", str(include_dir), "-I", str(cuda_include),
+               str(TRT_DIR / f"{name}.cpp"), "-o", str(target), f"-L{PACKAGE_DIR}",
+               "-l:libfga_attention.so", f"-Wl,-rpath,{rpath}", *extra]
+        subprocess.run(cmd, check=True)
+        built.append(target)
+    return built
 
 
 def main() -> None:

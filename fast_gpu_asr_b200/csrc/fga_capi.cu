@@ -13,6 +13,7 @@
 
 #include "../../include/fga_attention.h"
 #include "fga_kernels.h"
+#include "host_util.h"
 
 namespace {
 
@@ -21,6 +22,8 @@ constexpr int64_t kInt64Max = std::numeric_limits<int64_t>::max();
 constexpr float kLog2e = 1.4426950408889634f;
 
 thread_local const char* t_last_variant = "none";
+thread_local uint64_t t_wait_limit_ns = 0;  // 0: the kernels' default
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;  // 2 s, as sm100::kWaitLimitNs
 
 bool is_float_type(int32_t t) { return t == FGA_FLOAT || t == FGA_HALF || t == FGA_BF16; }
 
@@ -223,6 +226,15 @@ int32_t check_fused(const fga_tensor_desc* in, int32_t nin, const fga_tensor_des
     return FGA_SUCCESS;
 }
 
+// The work-counter workspace of the Zipformer weights and fused entry points: present,
+// large enough and aligned for 32-bit atomics.
+int32_t check_sched_workspace(void* workspace, size_t bytes) {
+    if (workspace == nullptr || bytes < FGA_SCHED_WORKSPACE_BYTES ||
+        (reinterpret_cast<uintptr_t>(workspace) & 3u) != 0)
+        return FGA_ERROR_WORKSPACE;
+    return FGA_SUCCESS;
+}
+
 // Common epilogue of every enqueue: report an earlier asynchronous error without
 // launching (parakeet…cu:948-952), launch, report the launch status.
 int32_t prior_error_status() {
@@ -230,6 +242,10 @@ int32_t prior_error_status() {
 }
 
 }  // namespace
+
+namespace fga {
+uint64_t wait_limit_ns() { return t_wait_limit_ns != 0 ? t_wait_limit_ns : kDefaultWaitLimitNs; }
+}  // namespace fga
 
 extern "C" {
 
@@ -247,11 +263,27 @@ const char* fga_status_string(int32_t status) {
         case FGA_ERROR_LAUNCH: return "kernel launch failed";
         case FGA_ERROR_NO_DEVICE: return "current CUDA device is not sm_100";
         case FGA_ERROR_UNSUPPORTED: return "outside this entry point's supported envelope";
+        case FGA_ERROR_WORKSPACE: return "workspace missing, smaller than required or misaligned";
+        case FGA_ERROR_DEVICE_ABORT:
+            return "a kernel on this device gave up a bounded wait; its outputs are incomplete";
         default: return "unknown status";
     }
 }
 
 const char* fga_last_kernel_variant(void) { return t_last_variant; }
+
+int32_t fga_device_status(void* stream, int32_t clear, uint32_t* detail) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaSuccess;
+    const uint32_t p = fga::take_parakeet_tc_error(s, clear != 0, &err);
+    const uint32_t z = fga::take_zipformer_tc_error(s, clear != 0, &err);
+    const uint32_t v = fga::take_value_tc_error(s, clear != 0, &err);
+    if (detail != nullptr) *detail = (p & 0xFFu) | ((z & 0xFFu) << 8) | ((v & 0xFFu) << 16);
+    if (err != cudaSuccess) return FGA_ERROR_PRIOR_CUDA_ERROR;
+    return (p | z | v) != 0u ? FGA_ERROR_DEVICE_ABORT : FGA_SUCCESS;
+}
+
+void fga_debug_set_wait_limit_ns(uint64_t limit_ns) { t_wait_limit_ns = limit_ns; }
 
 // ---- parakeet -----------------------------------------------------------------------
 int32_t fga_parakeet_relative_attention_check(const fga_tensor_desc* in, int32_t nin,
@@ -299,26 +331,28 @@ int32_t fga_zipformer_relative_attention_check(const fga_tensor_desc* in, int32_
 }
 
 size_t fga_zipformer_relative_attention_workspace_size(const fga_tensor_desc*, int32_t) {
-    return 0;
+    return FGA_SCHED_WORKSPACE_BYTES;  // the tensor-core kernel's work counter
 }
 
 int32_t fga_zipformer_relative_attention_enqueue(const fga_tensor_desc* in,
                                                  const fga_tensor_desc* out,
                                                  const void* const* inputs,
-                                                 void* const* outputs, void*, size_t,
-                                                 void* stream) {
+                                                 void* const* outputs, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
     fga::ZipformerWeightsProblem p{};
     int32_t st = check_zipformer(in, 3, out, 1, &p);
     if (st != FGA_SUCCESS) return st;
     if (inputs == nullptr || outputs == nullptr || outputs[0] == nullptr ||
         inputs[0] == nullptr || inputs[1] == nullptr || inputs[2] == nullptr)
         return FGA_ERROR_NULL_POINTER;
+    if ((st = check_sched_workspace(workspace, workspace_bytes)) != FGA_SUCCESS) return st;
     if ((st = prior_error_status()) != FGA_SUCCESS) return st;
     if (!fga::device_is_sm100()) return FGA_ERROR_NO_DEVICE;
     p.projection = inputs[0];
     p.position = inputs[1];
     p.mask = static_cast<const uint8_t*>(inputs[2]);
     p.weights = outputs[0];
+    p.sched = static_cast<unsigned int*>(workspace);
     const char* variant = "none";
     cudaError_t e =
         fga::launch_zipformer_weights(p, static_cast<cudaStream_t>(stream), &variant);
@@ -366,9 +400,14 @@ int32_t fga_zipformer_attention_fused_check(const fga_tensor_desc* in, int32_t n
     return check_fused(in, nin, out, nout, nullptr);
 }
 
+size_t fga_zipformer_attention_fused_workspace_size(const fga_tensor_desc*, int32_t) {
+    return FGA_SCHED_WORKSPACE_BYTES;  // the kernel's work counter
+}
+
 int32_t fga_zipformer_attention_fused_enqueue(const fga_tensor_desc* in,
                                               const fga_tensor_desc* out,
                                               const void* const* inputs, void* const* outputs,
+                                              void* workspace, size_t workspace_bytes,
                                               void* stream) {
     fga::ZipformerFusedProblem p{};
     int32_t st = check_fused(in, 5, out, 3, &p);
@@ -378,6 +417,7 @@ int32_t fga_zipformer_attention_fused_enqueue(const fga_tensor_desc* in,
         if (inputs[i] == nullptr) return FGA_ERROR_NULL_POINTER;
     for (int i = 0; i < 3; ++i)
         if (outputs[i] == nullptr) return FGA_ERROR_NULL_POINTER;
+    if ((st = check_sched_workspace(workspace, workspace_bytes)) != FGA_SUCCESS) return st;
     if ((st = prior_error_status()) != FGA_SUCCESS) return st;
     if (!fga::device_is_sm100()) return FGA_ERROR_NO_DEVICE;
     p.projection = inputs[0];
@@ -388,6 +428,7 @@ int32_t fga_zipformer_attention_fused_enqueue(const fga_tensor_desc* in,
     p.output1 = outputs[0];
     p.output2 = outputs[1];
     p.weights0 = outputs[2];
+    p.sched = static_cast<unsigned int*>(workspace);
     const cudaError_t e = fga::launch_zipformer_fused(p, static_cast<cudaStream_t>(stream));
     if (e == cudaErrorNotSupported) return FGA_ERROR_UNSUPPORTED;  // buffer alignment
     if (e != cudaSuccess) return FGA_ERROR_LAUNCH;

@@ -26,6 +26,7 @@ struct ZipformerWeightsProblem {
     const void* position;    // [1, 2T-1, H, 4]
     const uint8_t* mask;     // [N, T] bool
     void* weights;           // [N, H, T, T]
+    unsigned int* sched;     // tensor-core path: the launch's work counter (workspace)
     int32_t batch, length, heads, query_dim;
     int32_t dtype;
 };
@@ -42,6 +43,7 @@ struct ZipformerFusedProblem {
     void* output1;           // [N, T, H*vd]
     void* output2;           // [N, T, H*vd]
     void* weights0;          // [N, 1, T, T]: head 0's weights
+    unsigned int* sched;     // the launch's work counter (workspace)
     int32_t batch, length, heads, query_dim, value_dim;
     int32_t dtype;
 };
@@ -77,5 +79,12 @@ cudaError_t launch_zipformer_value_tc(const ZipformerValueProblem& p, cudaStream
 
 // True when the current device is sm_100 (the only target of this library).
 bool device_is_sm100();
+
+// Per-device error words of the tensor-core kernels (nonzero: a bounded wait gave up, or
+// a launch found its shared memory misaligned), read after the work queued on `stream`
+// and optionally cleared. CUDA errors of the reads go to *err.
+uint32_t take_parakeet_tc_error(cudaStream_t stream, bool clear, cudaError_t* err);
+uint32_t take_zipformer_tc_error(cudaStream_t stream, bool clear, cudaError_t* err);
+uint32_t take_value_tc_error(cudaStream_t stream, bool clear, cudaError_t* err);
 
 }  // namespace fga

@@ -55,6 +55,7 @@
 
 #include "fga_common.cuh"
 #include "fga_kernels.h"
+#include "host_util.h"
 #include "sm100_ptx.cuh"
 
 namespace fga {
@@ -104,6 +105,8 @@ enum : uint32_t {
 static_assert(kBarBEmpty0 + 2 == kNumBars, "barrier table");
 static_assert(kSmemBias % 16 == 0 && kSmemBytes <= 227 * 1024, "shared-memory map");
 
+// Per-device error word of this file's kernel: 1 = a bounded wait gave up, 2 = the dynamic
+// shared memory was not 1024-byte aligned. Read and cleared by fga_device_status.
 __device__ unsigned int g_parakeet_tc_error = 0;
 
 template <typename T> struct Fmt;
@@ -752,34 +755,6 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
 }
 
 // ---- host side ------------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return static_cast<EncodeTiledFn>(nullptr);
-        return reinterpret_cast<EncodeTiledFn>(p);
-    }();
-    return fn;
-}
-
-int sm_count() {
-    static int count = [] {
-        int dev = 0, n = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        return n > 0 ? n : 148;
-    }();
-    return count;
-}
-
 template <typename T>
 cudaError_t parakeet_tc_typed(const ParakeetProblem& p, cudaStream_t stream) {
     EncodeTiledFn encode = encode_fn();
@@ -824,16 +799,15 @@ cudaError_t parakeet_tc_typed(const ParakeetProblem& p, cudaStream_t stream) {
             CUDA_SUCCESS)
             return cudaErrorNotSupported;
     }
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(parakeet_tc_kernel<T>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBytes));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static SmemAttr attr;
+    if (cudaError_t e = attr.ensure(reinterpret_cast<const void*>(parakeet_tc_kernel<T>),
+                                    static_cast<int>(kSmemBytes));
+        e != cudaSuccess)
+        return e;
     const int64_t items = static_cast<int64_t>((p.length + kM - 1) / kM) * p.heads * p.batch;
-    const dim3 grid(static_cast<unsigned>(items < sm_count() ? items : sm_count()));
+    const int sms = sm_count();
+    if (sms <= 0) return cudaErrorNotSupported;
+    const dim3 grid(static_cast<unsigned>(items < sms ? items : sms));
     parakeet_tc_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(
         qkv_map, pos_map, out_map, static_cast<const T*>(p.content_bias),
         static_cast<const T*>(p.position_bias), p.valid_lengths, static_cast<T*>(p.output),
@@ -844,6 +818,10 @@ cudaError_t parakeet_tc_typed(const ParakeetProblem& p, cudaStream_t stream) {
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 }  // namespace
+
+uint32_t take_parakeet_tc_error(cudaStream_t stream, bool clear, cudaError_t* err) {
+    return take_error_word(g_parakeet_tc_error, stream, clear, err);
+}
 
 cudaError_t launch_parakeet_tc(const ParakeetProblem& p, cudaStream_t stream) {
     if (p.head_dim != kD || (p.dtype != FGA_HALF && p.dtype != FGA_BF16)) return cudaErrorNotSupported;

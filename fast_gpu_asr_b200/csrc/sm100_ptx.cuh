@@ -1,9 +1,10 @@
 // Thin inline-PTX layer for the sm_100a kernels: mbarriers with bounded waits, TMA
 // tile loads, and tcgen05 (TMEM allocation, UMMA issue/commit, TMEM load/store).
 //
-// Every wait here is bounded: after kWaitLimitNs of polling it gives up and returns
-// false, and the caller records a device error (see device_error below) and tears the
-// CTA down instead of spinning forever.
+// Every wait here is bounded: after its time limit (kWaitLimitNs unless the caller passes
+// another) it gives up and returns false; the kernel then records the timeout in its
+// per-device error word (read by fga_device_status) and tears the CTA down instead of
+// spinning forever.
 #pragma once
 
 #include <cuda.h>
@@ -51,12 +52,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Wait for phase `parity` of the barrier to complete; false after the time limit.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Wait for phase `parity` of the barrier to complete; false once `limit_ns` have passed.
+// The main loops of the kernels pass their launch's limit (a kernel parameter, 2 s unless
+// a test shortens it); teardown waits for copies and MMAs in flight keep the default, so
+// a shortened limit never lets a CTA exit while its own asynchronous work is pending.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = global_timer_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (global_timer_ns() - start > kWaitLimitNs) return false;
+        if (global_timer_ns() - start > limit_ns) return false;
     }
     return true;
 }

@@ -43,6 +43,7 @@
 
 #include "fga_common.cuh"
 #include "fga_kernels.h"
+#include "host_util.h"
 #include "sm100_ptx.cuh"
 
 namespace fga {
@@ -66,6 +67,8 @@ constexpr uint32_t kMaxVStages = 8;   // streaming V ring
 constexpr uint32_t kMaxVRes = 16;     // resident V: chunks per row (keys <= 1024)
 constexpr uint32_t kBarBytes = 512;
 
+// Per-device error word of this file's kernel: 1 = a bounded wait gave up, 2 = the dynamic
+// shared memory was not 1024-byte aligned. Read and cleared by fga_device_status.
 __device__ unsigned int g_value_tc_error = 0;
 
 template <typename T> struct Fmt;
@@ -161,7 +164,7 @@ struct Bars {  // mbarrier addresses (shared window); the TMEM slot and abort wo
     __device__ uint32_t v_full(uint32_t s) const { return base + 176 + 8 * s; }        // <= 16
     __device__ uint32_t v_empty(uint32_t s) const { return base + 304 + 8 * s; }
 };
-constexpr uint32_t kTmemSlotOff = 432, kAbortOff = 436;
+constexpr uint32_t kTmemSlotOff = 432, kAbortOff = 436, kDrainOff = 440;
 
 // Bounded wait with a warp-uniform result; a failure raises the CTA's abort word.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
@@ -273,6 +276,7 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
             mbar_init(B.v_full(s), 1);
             mbar_init(B.v_empty(s), 1);
         }
+        mbar_init(sbase + L.bar + kDrainOff, 1);
         *abort = 0u;
         fence_mbar_init();
         prefetch_tensormap(&v_map);
@@ -293,6 +297,7 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
         cur.init(t_begin, value_heads, nqb);
         Ring rs;
         int gs = 0;
+        uint32_t issued = 0, issued_par = 0;  // per raw slot: loaded, and that load's parity
 #pragma unroll 1
         for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
             const int ha = value_heads == 1 ? 0 : cur.h;
@@ -312,8 +317,19 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
                                 static_cast<int32_t>(R >> 3));
                 }
                 __syncwarp();
+                issued |= 1u << rs.slot;
+                issued_par = (issued_par & ~(1u << rs.slot)) | (rs.phase << rs.slot);
             }
         }
+        // Teardown (default time limit): every slot's last load has landed before shared
+        // memory is released. Without an abort the consumers already waited for them all.
+        if (lane == 0) {
+            bool ok = true;
+            for (uint32_t st = 0; st < L.raw_stages; ++st)
+                if ((issued >> st) & 1u) ok = mbar_wait(B.raw_full(st), (issued_par >> st) & 1u) && ok;
+            if (!ok) atomicExch(&g_value_tc_error, 1u);
+        }
+        __syncwarp();
     } else if (warp == 6) {
         // ---------------- V producer ----------------
         // Resident: at the start of each run of tiles of one (n, h), chunk c's stage c is
@@ -323,6 +339,7 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
         cur.init(t_begin, value_heads, nqb);
         Ring vr;
         int run = 0, g = 0;
+        uint32_t issued = 0, issued_par = 0;  // per V stage: loaded, and that load's parity
 #pragma unroll 1
         for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
             const bool run_start = i == 0 || cur.qb == 0;
@@ -330,17 +347,21 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
             const int col_base = (cur.h * hd) & ~7;
 #pragma unroll 1
             for (int c = 0; c < nchunks; ++c, ++g) {
-                uint32_t vs;
+                uint32_t vs, vpar;
                 bool ok;
                 if (L.vres) {
                     vs = static_cast<uint32_t>(c);
+                    vpar = static_cast<uint32_t>(run & 1);
                     ok = run == 0 || warp_wait(B.v_empty(vs), (run - 1) & 1, abort);
                 } else {
                     vs = vr.slot;
+                    vpar = vr.phase;
                     ok = g < static_cast<int>(L.v_stages) ||
                          warp_wait(B.v_empty(vs), vr.phase ^ 1u, abort);
                     vr.next(L.v_stages);
                 }
+                // (the first loads of a run skip the wait: check the abort word for them too)
+                ok = ok && __all_sync(0xffffffffu, *abort == 0u);
                 if (ok && lane == 0) {
                     mbar_expect_tx(B.v_full(vs), L.vstage);
                     for (int x = 0; x < cpad / static_cast<int>(L.vw); ++x)
@@ -349,9 +370,21 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
                                     cur.n);
                 }
                 __syncwarp();
+                if (ok) {
+                    issued |= 1u << vs;
+                    issued_par = (issued_par & ~(1u << vs)) | (vpar << vs);
+                }
             }
             ++run;
         }
+        // Teardown (default time limit): every stage's last load has landed.
+        if (lane == 0) {
+            bool ok = true;
+            for (uint32_t st = 0; st < L.v_stages; ++st)
+                if ((issued >> st) & 1u) ok = mbar_wait(B.v_full(st), (issued_par >> st) & 1u) && ok;
+            if (!ok) atomicExch(&g_value_tc_error, 1u);
+        }
+        __syncwarp();
     } else if (warp == 5) {
         // ---------------- MMA issuer ----------------
         // V: MN-major atoms of vw channels, vatom bytes apart along N; 8-key groups of
@@ -368,7 +401,6 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
         cur.init(t_begin, value_heads, nqb);
         Ring ar, vr, acc;
         int run = -1;
-        uint32_t last_slot = 0, last_phase = 0;
 #pragma unroll 1
         for (int i = 0; i < my_tiles; ++i, cur.next(value_heads, nqb)) {
             const bool run_start = i == 0 || cur.qb == 0;
@@ -387,8 +419,6 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
                 if (!L.vres) vr.next(L.v_stages);
                 bool ok = tile_ok && warp_wait(B.a_full(ar.slot), ar.phase, abort);
                 if (wait_v) ok = ok && warp_wait(B.v_full(vs), vph, abort);
-                last_slot = ar.slot;
-                last_phase = ar.phase;
                 if (!ok) continue;
                 tc_fence_after();
                 if (elect_one()) {
@@ -410,9 +440,15 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
             }
             acc.next(L.acc_bufs);
         }
-        // Teardown: every MMA of this CTA completes before TMEM is released.
-        if (!mbar_wait(B.a_empty(last_slot), last_phase) && lane == 0)
-            atomicExch(&g_value_tc_error, 1u);
+        // Teardown: every MMA of this CTA completes before TMEM is released (one commit
+        // tracks all MMAs this thread issued, including when some were skipped after an abort).
+        bool drained = true;
+        if (elect_one()) {
+            umma_commit(sbase + L.bar + kDrainOff);
+            drained = mbar_wait(sbase + L.bar + kDrainOff, 0);
+        }
+        __syncwarp();
+        if (!drained) atomicExch(&g_value_tc_error, 1u);
     } else if (warp >= 7 && warp <= 10) {
         // ---------------- epilogue warps 7..10 ----------------
         const int qtr = warp & 3;
@@ -551,32 +587,6 @@ zipformer_value_tc_kernel(const __grid_constant__ CUtensorMap v_map,
 }
 
 // ---- host side ------------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return static_cast<EncodeTiledFn>(nullptr);
-        return reinterpret_cast<EncodeTiledFn>(p);
-    }();
-    return fn;
-}
-
-int sm_count() {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return 0;
-    return n;
-}
-
 template <typename T>
 cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_t stream) {
     EncodeTiledFn encode = encode_fn();
@@ -600,14 +610,11 @@ cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_
                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
         CUDA_SUCCESS)
         return cudaErrorNotSupported;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(zipformer_value_tc_kernel<T>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemLimit));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static SmemAttr attr;
+    if (cudaError_t e = attr.ensure(reinterpret_cast<const void*>(zipformer_value_tc_kernel<T>),
+                                    static_cast<int>(kSmemLimit));
+        e != cudaSuccess)
+        return e;
     // Attention rows by residue class r = R mod 8 of the flattened row index R: class r's
     // rows start at element r*T + 8*T*m; its map begins at the 16-byte boundary below r*T.
     AMaps amaps;
@@ -640,6 +647,10 @@ cudaError_t value_tc_typed(const ZipformerValueProblem& p, int cpad, cudaStream_
 }
 
 }  // namespace
+
+uint32_t take_value_tc_error(cudaStream_t stream, bool clear, cudaError_t* err) {
+    return take_error_word(g_value_tc_error, stream, clear, err);
+}
 
 cudaError_t launch_zipformer_value_tc(const ZipformerValueProblem& p, cudaStream_t stream) {
     if (p.dtype != FGA_HALF && p.dtype != FGA_BF16) return cudaErrorNotSupported;

@@ -40,11 +40,11 @@
 // output type).
 #include <cuda.h>
 
-#include <atomic>
 #include <cstdint>
 
 #include "fga_common.cuh"
 #include "fga_kernels.h"
+#include "host_util.h"
 #include "sm100_ptx.cuh"
 
 namespace fga {
@@ -83,9 +83,8 @@ constexpr int kPiece = 64;
 constexpr int kStageRow = 16 + kPiece * 2;
 constexpr int kStageWarp = 32 * kStageRow;
 
-// Dynamic pair scheduling: each launch takes one of kSchedSlots (work, done) counter
-// pairs round-robin; the last CTA of a launch resets its pair to zero.
-constexpr int kSchedSlots = 64;
+// Dynamic pair scheduling: the CTAs draw pairs from one 32-bit counter in the caller's
+// workspace, which the launcher zeroes on the launch's stream just before the kernel.
 
 // Fused variant (weights applied to two value tensors in the same kernel): pass 2 writes
 // each 64-key piece of rounded weights into a P tile (one per warp sub-slot, 128 rows x
@@ -123,8 +122,9 @@ static_assert(SmemEnd<false>::bytes <= 227 * 1024 && SmemEnd<true>::bytes <= 227
               "shared memory budget");
 static_assert(kMaxT / kM <= kComputeWarps, "one warp per query block computes its liveness");
 
+// Per-device error word of this file's kernels: 1 = a bounded wait gave up, 2 = the
+// dynamic shared memory was not 1024-byte aligned. Read and cleared by fga_device_status.
 __device__ unsigned int g_zipformer_tc_error = 0;
-__device__ unsigned int g_zipformer_sched[2 * kSchedSlots];
 
 template <typename T> struct Fmt;
 template <> struct Fmt<__half> { static constexpr uint32_t v = 0; };
@@ -191,8 +191,8 @@ __device__ __forceinline__ uint64_t sw64_desc(uint32_t smem_addr) {
 // Bounded wait with a warp-uniform result; a failure raises the CTA's abort word (the
 // CTA then skips all further work but keeps every barrier, so no thread is stranded).
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
-                                          volatile uint32_t* abort) {
-    bool ok = (*abort == 0u) && mbar_wait(bar, parity);
+                                          volatile uint32_t* abort, uint64_t limit_ns) {
+    bool ok = (*abort == 0u) && mbar_wait(bar, parity, limit_ns);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok && (threadIdx.x & 31) == 0) {
         *abort = 1u;
@@ -274,7 +274,8 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             const T* __restrict__ proj, const T* __restrict__ pos,
                             const uint8_t* __restrict__ mask, T* __restrict__ out,
                             T* __restrict__ out1, T* __restrict__ out2, int seq, int heads,
-                            int vd, int num_pairs, int slot) {
+                            int vd, int num_pairs, unsigned int* __restrict__ sched,
+                            uint64_t wait_limit) {
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr uint32_t kSmemBar = SmemEnd<kFused>::bar;
     const uint32_t sbase = smem_u32(smem);
@@ -285,6 +286,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + kSmemBar + 44);
     uint16_t* band = reinterpret_cast<uint16_t*>(smem + kSmemBand);
     volatile int* next_pair = reinterpret_cast<volatile int*>(smem + kSmemBar + 48);  // [2]
+    const uint32_t bar_drain = sbase + kSmemBar + 56;  // teardown: every MMA completed
     // Fused variant only.
     const uint32_t bar_a_full = sbase + kSmemBar + 64;    // + 8 * sub-slot
     const uint32_t bar_a_empty = sbase + kSmemBar + 80;   // + 8 * sub-slot
@@ -319,6 +321,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         mbar_init(bar_full + 8, 1);
         mbar_init(bar_free, kComputeWarps);
         mbar_init(bar_free + 8, kComputeWarps);
+        mbar_init(bar_drain, 1);
         if constexpr (kFused) {
             for (int i = 0; i < kSub; ++i) {
                 mbar_init(bar_a_full + 8 * i, 4);  // the sub-slot's four warps
@@ -370,7 +373,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         kq_pair = p;
     };
     // Pair tickets are drawn one pair ahead, so the atomic's round trip overlaps the work.
-    if (tid == 0) next_pair[0] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
+    if (tid == 0) next_pair[0] = static_cast<int>(atomicAdd(sched, 1u));
 #pragma unroll 1
     for (int iter = 0;; ++iter) {
         named_barrier(1, kThreads);
@@ -378,7 +381,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         if (pair >= num_pairs) break;
         // Every thread read slot (iter+1)&1 of the previous pair before this barrier.
         if (tid == 0)
-            next_pair[(iter + 1) & 1] = static_cast<int>(atomicAdd(&g_zipformer_sched[2 * slot], 1u));
+            next_pair[(iter + 1) & 1] = static_cast<int>(atomicAdd(sched, 1u));
         const int n = pair / heads;
         const int h = pair - n * heads;
         const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
@@ -426,7 +429,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         } else if (ucount > 0) {
             // Q/K of the previous pair are read by its MMAs: wait for the last one.
             const uint32_t u = ucount - 1;
-            warp_wait(bar_full + 8 * (u & 1), (u >> 1) & 1, abort);
+            warp_wait(bar_full + 8 * (u & 1), (u >> 1) & 1, abort, wait_limit);
         }
         named_barrier(1, kThreads);  // mask information of this pair is visible
 
@@ -441,8 +444,8 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             // The loads were normally issued one pair ahead (end of the previous pair).
             if (kq_pair != pair && live_mask != 0u && __all_sync(0xffffffffu, *abort == 0u))
                 load_qk(pair);
-            if (kq_pair == pair) {
-                warp_wait(bar_kq, kq_phase & 1, abort);
+            if (kq_pair == pair && warp_wait(bar_kq, kq_phase & 1, abort, wait_limit)) {
+                // (After a failed wait the loads stay in flight: teardown drains them.)
                 ++kq_phase;
                 kq_pair = -1;
             }
@@ -451,7 +454,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 // previous pair's last P.V MMAs have read theirs. They land under pass 1.
                 if (live_mask != 0u && __all_sync(0xffffffffu, *abort == 0u)) {
                     bool ok = true;
-                    if (o_fulls > 0) ok = warp_wait(bar_o_full, (o_fulls - 1) & 1, abort);
+                    if (o_fulls > 0) ok = warp_wait(bar_o_full, (o_fulls - 1) & 1, abort, wait_limit);
                     if (ok) {
                         if (lane == 0) {
                             const int nvb = (seq + kVBox - 1) / kVBox;
@@ -479,11 +482,11 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     const uint32_t u = ucount + j;
                     const uint32_t sb = u & 1;
                     bool ok = __all_sync(0xffffffffu, *abort == 0u);
-                    if (ok && u >= 2) ok = warp_wait(bar_free + 8 * sb, ((u >> 1) - 1) & 1, abort);
+                    if (ok && u >= 2) ok = warp_wait(bar_free + 8 * sb, ((u >> 1) - 1) & 1, abort, wait_limit);
                     if constexpr (kFused) {
                         // This buffer holds the accumulators of an earlier output tile.
                         if (ok && static_cast<int>(sb) == o_buf) {
-                            ok = warp_wait(bar_o_free, o_frees & 1, abort);
+                            ok = warp_wait(bar_o_free, o_frees & 1, abort, wait_limit);
                             ++o_frees;
                             o_buf = -1;
                         }
@@ -508,14 +511,16 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     constexpr uint32_t idesc_pv = idesc_f16(Fmt<T>::v, kM, 16, 0, 1);
                     bool ok = __all_sync(0xffffffffu, *abort == 0u);
                     if (ok && o_buf >= 0) {
-                        ok = warp_wait(bar_o_free, o_frees & 1, abort);
+                        ok = warp_wait(bar_o_free, o_frees & 1, abort, wait_limit);
                         ++o_frees;
                         o_buf = -1;
                     }
                     if (ok && v_pending) {
-                        ok = warp_wait(bar_v_full, v_waits & 1, abort);
-                        ++v_waits;
-                        v_pending = false;
+                        ok = warp_wait(bar_v_full, v_waits & 1, abort, wait_limit);
+                        if (ok) {  // otherwise the loads stay in flight: teardown drains them
+                            ++v_waits;
+                            v_pending = false;
+                        }
                     }
                     const uint32_t ob = (ucount & 1u) ^ 1u;
                     const int cnt[kSub] = {split, npieces - split};
@@ -527,7 +532,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                         for (int sl = 0; sl < kSub; ++sl) {
                             if (i >= cnt[sl]) continue;
                             const int piece = sl == 0 ? i : split + i;
-                            if (ok) ok = warp_wait(bar_a_full + 8 * sl, a_uses[sl] & 1, abort);
+                            if (ok) ok = warp_wait(bar_a_full + 8 * sl, a_uses[sl] & 1, abort, wait_limit);
                             if (ok) {
                                 tc_fence_after();
                                 if (elect_one()) {
@@ -566,7 +571,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 bool ok = true;
                 if (ucount > 0) {
                     const uint32_t u = ucount - 1;
-                    ok = warp_wait(bar_full + 8 * (u & 1), (u >> 1) & 1, abort);
+                    ok = warp_wait(bar_full + 8 * (u & 1), (u >> 1) & 1, abort, wait_limit);
                 }
                 if (ok) load_qk(nxt);
             }
@@ -649,7 +654,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     const int g = 2 * j + sub;
                     const uint32_t vb = g < ngroups ? valid[g] : 0u;
                     const bool math = warp_live && vb != 0u;
-                    const bool ok = warp_wait(bar_full + 8 * sb, (u >> 1) & 1, abort);
+                    const bool ok = warp_wait(bar_full + 8 * sb, (u >> 1) & 1, abort, wait_limit);
                     uint32_t r[32];
                     if (ok && math) {
                         tmem_ld32(tmem + lane_off + sb * kChunk + sub * kGroup, r);
@@ -834,7 +839,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 if constexpr (kFused) {
                     // The piece's rounded weights go to this sub-slot's P tile (row q_local,
                     // keys k0..k0+63) once the control warp's previous P.V has read it.
-                    if (p_uses > 0) warp_wait(bar_a_empty + 8 * sub, (p_uses - 1) & 1, abort);
+                    if (p_uses > 0) warp_wait(bar_a_empty + 8 * sub, (p_uses - 1) & 1, abort, wait_limit);
                     uint8_t* pt = smem + kSmemP + sub * kPTile;
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
@@ -903,7 +908,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 // O row of this warp's value tensor: accumulator columns of the block's last
                 // score buffer, rounded to T like the attention-value plugin's output.
                 const uint32_t ocol = ((ucount & 1u) ^ 1u) * kChunk + sub * 16;
-                const bool ok = warp_wait(bar_o_full, o_fulls & 1, abort);
+                const bool ok = warp_wait(bar_o_full, o_fulls & 1, abort, wait_limit);
                 ++o_fulls;
                 uint32_t r[16];
                 if (ok) {
@@ -933,26 +938,22 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         }
     }
 
-    // Teardown: the control warp waits (bounded) for its last MMA before TMEM is freed,
-    // and for Q/K loads still in flight (only after an abort) before shared memory is.
-    if (control && ucount > 0) {
-        const uint32_t u = ucount - 1;
-        if (!mbar_wait(bar_full + 8 * (u & 1), (u >> 1) & 1) && lane == 0)
-            atomicExch(&g_zipformer_tc_error, 1u);
-    }
-    if (control && kq_pair >= 0) {
-        if (!mbar_wait(bar_kq, kq_phase & 1) && lane == 0) atomicExch(&g_zipformer_tc_error, 1u);
-    }
-    if constexpr (kFused) {
-        // P.V MMAs and V loads (the latter only outstanding after an abort).
-        if (control && o_fulls > 0) {
-            if (!mbar_wait(bar_o_full, (o_fulls - 1) & 1) && lane == 0)
-                atomicExch(&g_zipformer_tc_error, 1u);
+    // Teardown, with the default time limit whatever the launch's: the control warp waits
+    // for every MMA it issued (one commit tracks them all, so MMAs skipped after an abort
+    // do not matter) before TMEM is freed, and for TMA loads still in flight (only after
+    // an abort) before shared memory is.
+    if (control) {
+        bool ok = true;
+        if (elect_one()) {
+            umma_commit(bar_drain);
+            ok = mbar_wait(bar_drain, 0);
         }
-        if (control && v_pending) {
-            if (!mbar_wait(bar_v_full, v_waits & 1) && lane == 0)
-                atomicExch(&g_zipformer_tc_error, 1u);
+        __syncwarp();
+        if (kq_pair >= 0) ok = mbar_wait(bar_kq, kq_phase & 1) && ok;
+        if constexpr (kFused) {
+            if (v_pending) ok = mbar_wait(bar_v_full, v_waits & 1) && ok;
         }
+        if (!ok) atomicExch(&g_zipformer_tc_error, 1u);
     }
     tc_fence_before();
     __syncthreads();
@@ -960,43 +961,9 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
-    if (tid == 0) {
-        // Every CTA has drawn past the last pair; the last one out resets the slot.
-        __threadfence();
-        if (atomicAdd(&g_zipformer_sched[2 * slot + 1], 1u) == gridDim.x - 1) {
-            atomicExch(&g_zipformer_sched[2 * slot], 0u);
-            atomicExch(&g_zipformer_sched[2 * slot + 1], 0u);
-        }
-    }
 }
 
 // ---- host side ------------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return static_cast<EncodeTiledFn>(nullptr);
-        return reinterpret_cast<EncodeTiledFn>(p);
-    }();
-    return fn;
-}
-
-int sm_count() {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return 0;
-    return n;
-}
-
 CUtensorMapDataType map_type(int32_t dtype) {
     return dtype == FGA_HALF ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 }
@@ -1032,20 +999,15 @@ bool encode_value_map(EncodeTiledFn encode, CUtensorMap* map, const void* value,
 
 template <typename T, bool kFused>
 cudaError_t set_smem_attr() {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(zipformer_weights_tc_kernel<T, kFused>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(SmemEnd<kFused>::bytes));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
-    return cudaSuccess;
+    static SmemAttr attr;
+    return attr.ensure(reinterpret_cast<const void*>(zipformer_weights_tc_kernel<T, kFused>),
+                       static_cast<int>(SmemEnd<kFused>::bytes));
 }
 
-int next_sched_slot() {
-    static std::atomic<unsigned int> ticket{0};
-    return static_cast<int>(ticket.fetch_add(1u) % kSchedSlots);
+// The work counter starts at zero for every launch: a 4-byte memset on the same stream,
+// ordered before the kernel (and captured with it in a CUDA graph).
+cudaError_t zero_counter(unsigned int* sched, cudaStream_t stream) {
+    return cudaMemsetAsync(sched, 0, sizeof(unsigned int), stream);
 }
 
 template <typename T>
@@ -1060,10 +1022,11 @@ cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stre
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
     const int grid = static_cast<int>(pairs < sms ? pairs : sms);
+    if (cudaError_t e = zero_counter(p.sched, stream); e != cudaSuccess) return e;
     zipformer_weights_tc_kernel<T, false><<<grid, kThreads, SmemEnd<false>::bytes, stream>>>(
         map, unused, unused, static_cast<const T*>(p.projection),
         static_cast<const T*>(p.position), p.mask, static_cast<T*>(p.weights), nullptr, nullptr,
-        p.length, p.heads, 0, static_cast<int>(pairs), next_sched_slot());
+        p.length, p.heads, 0, static_cast<int>(pairs), p.sched, wait_limit_ns());
     return cudaGetLastError();
 }
 
@@ -1082,15 +1045,20 @@ cudaError_t fused_tc_typed(const ZipformerFusedProblem& p, cudaStream_t stream) 
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
     const int grid = static_cast<int>(pairs < sms ? pairs : sms);
+    if (cudaError_t e = zero_counter(p.sched, stream); e != cudaSuccess) return e;
     zipformer_weights_tc_kernel<T, true><<<grid, kThreads, SmemEnd<true>::bytes, stream>>>(
         map, v1, v2, static_cast<const T*>(p.projection), static_cast<const T*>(p.position),
         p.mask, static_cast<T*>(p.weights0), static_cast<T*>(p.output1),
         static_cast<T*>(p.output2), p.length, p.heads, p.value_dim, static_cast<int>(pairs),
-        next_sched_slot());
+        p.sched, wait_limit_ns());
     return cudaGetLastError();
 }
 
 }  // namespace
+
+uint32_t take_zipformer_tc_error(cudaStream_t stream, bool clear, cudaError_t* err) {
+    return take_error_word(g_zipformer_tc_error, stream, clear, err);
+}
 
 cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem& p, cudaStream_t stream) {
     if (p.query_dim != kQd || (p.dtype != FGA_HALF && p.dtype != FGA_BF16))

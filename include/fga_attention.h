@@ -13,10 +13,14 @@
  * three plugin calls of one Zipformer layer at once) and follows the same conventions.
  *
  * Memory: the caller owns every input, output and workspace buffer; no entry point
- * allocates device memory, and none needs workspace (the `*_workspace_size` queries
- * return 0). All launches go on the given stream only, so an entry point is safe to
- * capture in a CUDA graph and safe to call from several host threads on different
- * streams at once.
+ * allocates device memory. The Zipformer weights and fused entry points need a small
+ * workspace (FGA_SCHED_WORKSPACE_BYTES, reported by their `*_workspace_size` queries):
+ * it holds the launch's work counter, which the entry point zeroes on the given stream
+ * before the kernel, so it needs no initialisation. The other entry points need none
+ * (their queries return 0). All launches go on the given stream only, so an entry point
+ * is safe to capture in a CUDA graph. Calls from several host threads on different
+ * streams may run at once as long as each call has its own workspace (TensorRT gives each
+ * execution context its own); two launches that share a workspace must not overlap.
  *
  * Error behaviour mirrors the reference plugins: descriptors are re-validated on every
  * call (rank, dtype, cross-input shape relations, 64-bit size arithmetic), a CUDA
@@ -39,7 +43,9 @@
 extern "C" {
 #endif
 
-#define FGA_ABI_VERSION 1
+#define FGA_ABI_VERSION 2
+/* Workspace of the Zipformer weights and fused entry points (at least 4-byte aligned). */
+#define FGA_SCHED_WORKSPACE_BYTES 256
 #define FGA_MAX_DIMS 8
 
 /* Element types. The values equal TensorRT's nvinfer1::DataType numbering, so a
@@ -65,6 +71,8 @@ enum fga_status {
     FGA_ERROR_LAUNCH = 7,
     FGA_ERROR_NO_DEVICE = 8,      /* current device is not sm_100 */
     FGA_ERROR_UNSUPPORTED = 9,    /* valid, but outside an entry point's stated envelope */
+    FGA_ERROR_WORKSPACE = 10,     /* workspace missing, too small or misaligned */
+    FGA_ERROR_DEVICE_ABORT = 11,  /* fga_device_status: a kernel gave up a bounded wait */
 };
 
 /* Mirrors nvinfer1::PluginTensorDesc minus format (row-major linear is implied). */
@@ -115,7 +123,8 @@ FGA_API int32_t fga_parakeet_relative_attention_enqueue(const fga_tensor_desc* i
  *
  * No scale is applied. Masked keys get weight 0, a row whose keys are all masked is
  * zero, and query rows q >= 7 with mask[q-7] set (the 7-frame padded-query halo) are
- * zero.
+ * zero. workspace: FGA_SCHED_WORKSPACE_BYTES (the reference reported 16 MB for cuBLAS,
+ * zipformer_relative_attention_plugin.cu:705-716); FGA_ERROR_WORKSPACE without it.
  * -------------------------------------------------------------------------------- */
 FGA_API int32_t fga_zipformer_relative_attention_check(const fga_tensor_desc* input_descs,
     int32_t nb_inputs, const fga_tensor_desc* output_descs, int32_t nb_outputs);
@@ -175,13 +184,15 @@ FGA_API int32_t fga_zipformer_attention_value_enqueue(const fga_tensor_desc* inp
  * path does; the products are accumulated in fp32. Envelope: f16/bf16, qd = 32, H even,
  * T <= 768, vd a multiple of 4 in [4, 16], H*vd*2 bytes a multiple of 16, value tensors
  * and weights0 16-byte aligned, outputs 4-byte aligned. Outside it the entry point
- * returns FGA_ERROR_UNSUPPORTED and launches nothing. It needs no workspace.
+ * returns FGA_ERROR_UNSUPPORTED and launches nothing. workspace: FGA_SCHED_WORKSPACE_BYTES.
  * -------------------------------------------------------------------------------- */
 FGA_API int32_t fga_zipformer_attention_fused_check(const fga_tensor_desc* input_descs,
     int32_t nb_inputs, const fga_tensor_desc* output_descs, int32_t nb_outputs);
+FGA_API size_t fga_zipformer_attention_fused_workspace_size(const fga_tensor_desc* input_descs,
+    int32_t nb_inputs);
 FGA_API int32_t fga_zipformer_attention_fused_enqueue(const fga_tensor_desc* input_descs,
     const fga_tensor_desc* output_descs, const void* const* inputs, void* const* outputs,
-    void* stream);
+    void* workspace, size_t workspace_bytes, void* stream);
 
 /* --------------------------------------------------------------------------------
  * Library identity and diagnostics (no counterpart needed in the reference; the
@@ -192,6 +203,22 @@ FGA_API const char* fga_status_string(int32_t status);
 /* Name of the kernel variant the last successful enqueue on this host thread chose
  * ("tcgen05", "simt", ...); for tests and benchmarks. */
 FGA_API const char* fga_last_kernel_variant(void);
+
+/* Device-side status of the tensor-core kernels on the current device. Every wait inside
+ * them is bounded (2 s); a kernel that gives up records it in a per-device error word and
+ * tears down, leaving its outputs incomplete, while enqueue has already returned success.
+ * This call waits for the work queued on `stream`, reads the words and, if `clear` is
+ * nonzero, resets them. Returns FGA_SUCCESS when no kernel gave up since the last clear,
+ * FGA_ERROR_DEVICE_ABORT when one did, FGA_ERROR_PRIOR_CUDA_ERROR when the read failed.
+ * `detail` (optional) receives the words: bits 0-7 Parakeet, 8-15 Zipformer weights and
+ * fused, 16-23 attention-value (1 = a wait gave up, 2 = misaligned shared memory). */
+FGA_API int32_t fga_device_status(void* stream, int32_t clear, uint32_t* detail);
+
+/* Test hook: the time limit (ns) of the bounded waits in the main loops of the Zipformer
+ * weights and fused kernels, for launches made later by this host thread; 0 restores the
+ * default (2 s). Waits that drain a CTA's own copies and MMAs keep the default, so a short
+ * limit makes the kernel give up cleanly, never fault. */
+FGA_API void fga_debug_set_wait_limit_ns(uint64_t limit_ns);
 
 #ifdef __cplusplus
 }

@@ -47,16 +47,36 @@ def test_library_exports_every_declared_symbol(library):
 
 
 def test_status_strings(library):
-    for code in range(10):
+    for code in range(12):
         assert library.fga_status_string(code)
+        assert library.fga_status_string(code) != b"unknown status"
     assert library.fga_status_string(0) == b"success"
 
 
-def test_workspace_is_zero(library):
+def test_workspace_sizes(library):
+    """Parakeet and attention-value need none; the Zipformer weights and fused entry
+    points take the launch's work counter from the workspace."""
     descs = _lib.desc_array([D(F16, (2, 33, 384)), D(F16, (1, 65, 128))])
     assert library.fga_parakeet_relative_attention_workspace_size(descs, 2) == 0
-    assert library.fga_zipformer_relative_attention_workspace_size(descs, 2) == 0
     assert library.fga_zipformer_attention_value_workspace_size(descs, 2, 4) == 0
+    assert (library.fga_zipformer_relative_attention_workspace_size(descs, 2)
+            == _lib.SCHED_WORKSPACE_BYTES)
+    assert (library.fga_zipformer_attention_fused_workspace_size(descs, 2)
+            == _lib.SCHED_WORKSPACE_BYTES)
+    header = HEADER.read_text()
+    assert f"#define FGA_SCHED_WORKSPACE_BYTES {_lib.SCHED_WORKSPACE_BYTES}" in header
+
+
+def test_weights_enqueue_rejects_missing_workspace(library):
+    """Checked before any device work: null, short and misaligned workspaces."""
+    ins = _lib.desc_array([D(BF16, (2, 65, 272)), D(BF16, (1, 129, 4, 4)), D(BOOL, (2, 65))])
+    outs = _lib.desc_array([D(BF16, (2, 4, 65, 65))])
+    ptrs = _lib.pointer_array([256] * 3)
+    optr = _lib.pointer_array([256])
+    enqueue = library.fga_zipformer_relative_attention_enqueue
+    assert enqueue(ins, outs, ptrs, optr, None, 256, None) == 10
+    assert enqueue(ins, outs, ptrs, optr, 256, 255, None) == 10
+    assert enqueue(ins, outs, ptrs, optr, 258, 256, None) == 10
 
 
 # ---- parakeet contract ----------------------------------------------------------------
@@ -210,7 +230,9 @@ def fused_status(descs):
 
 def test_fused_header_declares_its_entry_points():
     names = declared_symbols()
-    assert {"fga_zipformer_attention_fused_check", "fga_zipformer_attention_fused_enqueue"} <= names
+    assert {"fga_zipformer_attention_fused_check", "fga_zipformer_attention_fused_workspace_size",
+            "fga_zipformer_attention_fused_enqueue"} <= names
+    assert {"fga_device_status", "fga_debug_set_wait_limit_ns"} <= names
 
 
 def test_fused_accepts_its_envelope(library):
@@ -262,9 +284,12 @@ def test_fused_enqueue_rejects_null_pointers(library):
     ptrs_in = _lib.pointer_array([16] * 4 + [None])
     ptrs_out = _lib.pointer_array([16] * 3)
     assert library.fga_zipformer_attention_fused_enqueue(in_arr, out_arr, ptrs_in, ptrs_out,
-                                                         None) == 1
+                                                         256, 256, None) == 1
     ptrs_in = _lib.pointer_array([16] * 5)
     ptrs_out = _lib.pointer_array([16, None, 16])
     assert library.fga_zipformer_attention_fused_enqueue(in_arr, out_arr, ptrs_in, ptrs_out,
-                                                         None) == 1
+                                                         256, 256, None) == 1
+    ptrs_out = _lib.pointer_array([16] * 3)
+    assert library.fga_zipformer_attention_fused_enqueue(in_arr, out_arr, ptrs_in, ptrs_out,
+                                                         None, 0, None) == 10
 

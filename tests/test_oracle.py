@@ -141,3 +141,32 @@ def test_oracle_composition_matches_reference_layer_outputs(path):
                            ("nonlin_value", "nonlin_out", 1)):
         got = zipformer_attention_value(w, g[value], vh, dt)
         np.testing.assert_allclose(got, g[out], rtol=tol, atol=tol)
+
+
+def test_weight_check_accepts_only_ambiguous_content_rounding():
+    """The full-size weight check allows an element outside the tolerance only when a
+    different rounding of an ambiguous content score (one whose exact value sits on a
+    midpoint between two bf16 values) reproduces its whole row."""
+    from oracle import zipformer_relative_attention as oracle_weights
+
+    heads, qd, t = 1, 32, 2
+    proj = np.zeros((1, t, heads * (2 * qd + 4)), np.float32)
+    proj[0, 0, 0], proj[0, 0, 1] = 1.0, 2.0**-4           # query 0
+    proj[0, 0, qd], proj[0, 0, qd + 1] = 16.0, 1.0         # key 0: score 16.0625, a midpoint
+    proj[0, 1, qd] = 15.0                                  # key 1: score 15
+    pos = np.zeros((1, 2 * t - 1, heads, 4), np.float32)
+    mask = np.zeros((1, t), bool)
+    expected = oracle_weights(proj, pos, mask, "bfloat16")
+    assert cases.assert_zipformer_weights_match(expected, expected, proj, pos, mask,
+                                                "bfloat16", heads) == 0
+    # The same row with the score rounded up to 16.125 instead of down to 16.
+    flipped = expected.copy()
+    row = np.exp(np.array([16.125, 15.0]) - 16.125)
+    flipped[0, 0, 0] = cases.quantize((row / row.sum()).astype(np.float32), "bfloat16")
+    assert np.abs(flipped - expected).max() > 1e-2
+    assert cases.assert_zipformer_weights_match(flipped, expected, proj, pos, mask,
+                                                "bfloat16", heads) == 1
+    wrong = expected.copy()
+    wrong[0, 0, 0] = [0.6, 0.4]
+    with pytest.raises(AssertionError):
+        cases.assert_zipformer_weights_match(wrong, expected, proj, pos, mask, "bfloat16", heads)
