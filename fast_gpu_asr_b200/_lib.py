@@ -77,6 +77,8 @@ SYMBOLS = {
     "fga_zipformer_relative_attention_enqueue": (
         ctypes.c_int32,
         (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP, ctypes.c_size_t, _VP)),
+    "fga_zipformer_relative_attention_enqueue_no_workspace": (
+        ctypes.c_int32, (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP)),
     "fga_zipformer_attention_value_check": (
         ctypes.c_int32, (_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int32)),
     "fga_zipformer_attention_value_workspace_size": (

@@ -361,6 +361,38 @@ int32_t fga_zipformer_relative_attention_enqueue(const fga_tensor_desc* in,
     return FGA_SUCCESS;
 }
 
+// Same computation without a workspace: the work counter comes from a file-scope device
+// array (FGA_NO_WORKSPACE_SCRATCH_BYTES) in the kernel's file, so nothing is allocated.
+int32_t fga_zipformer_relative_attention_enqueue_no_workspace(const fga_tensor_desc* in,
+                                                              const fga_tensor_desc* out,
+                                                              const void* const* inputs,
+                                                              void* const* outputs, void* stream) {
+    fga::ZipformerWeightsProblem p{};
+    int32_t st = check_zipformer(in, 3, out, 1, &p);
+    if (st != FGA_SUCCESS) return st;
+    if (inputs == nullptr || outputs == nullptr || outputs[0] == nullptr ||
+        inputs[0] == nullptr || inputs[1] == nullptr || inputs[2] == nullptr)
+        return FGA_ERROR_NULL_POINTER;
+    // The scratch this problem needs must fit the fixed array.
+    if (fga_zipformer_relative_attention_workspace_size(in, 3) > FGA_NO_WORKSPACE_SCRATCH_BYTES)
+        return FGA_ERROR_WORKSPACE;
+    if ((st = prior_error_status()) != FGA_SUCCESS) return st;
+    if (!fga::device_is_sm100()) return FGA_ERROR_NO_DEVICE;
+    void* scratch = nullptr;
+    if (fga::no_workspace_scratch(&scratch) != cudaSuccess) return FGA_ERROR_LAUNCH;
+    p.projection = inputs[0];
+    p.position = inputs[1];
+    p.mask = static_cast<const uint8_t*>(inputs[2]);
+    p.weights = outputs[0];
+    p.sched = static_cast<unsigned int*>(scratch);
+    const char* variant = "none";
+    cudaError_t e =
+        fga::launch_zipformer_weights(p, static_cast<cudaStream_t>(stream), &variant);
+    if (e != cudaSuccess) return FGA_ERROR_LAUNCH;
+    t_last_variant = variant;
+    return FGA_SUCCESS;
+}
+
 // ---- zipformer attention-value ----------------------------------------------------------
 int32_t fga_zipformer_attention_value_check(const fga_tensor_desc* in, int32_t nin,
                                             const fga_tensor_desc* out, int32_t nout,

@@ -66,6 +66,10 @@ cudaError_t launch_zipformer_value(const ZipformerValueProblem& p, cudaStream_t 
 // T <= 768, vd a multiple of 4 up to 16, H*vd a multiple of 8, aligned buffers).
 cudaError_t launch_zipformer_fused(const ZipformerFusedProblem& p, cudaStream_t stream);
 
+// Device address (current device) of the scratch that the weights entry point without a
+// workspace uses for its work counter (FGA_NO_WORKSPACE_SCRATCH_BYTES bytes).
+cudaError_t no_workspace_scratch(void** ptr);
+
 // SIMT (CUDA-core) kernels: every dtype and shape the contract accepts.
 cudaError_t launch_parakeet_simt(const ParakeetProblem& p, cudaStream_t stream);
 cudaError_t launch_zipformer_weights_simt(const ZipformerWeightsProblem& p, cudaStream_t stream);

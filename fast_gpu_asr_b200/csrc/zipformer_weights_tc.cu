@@ -40,6 +40,7 @@
 // output type).
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "fga_common.cuh"
@@ -1058,6 +1059,35 @@ cudaError_t fused_tc_typed(const ZipformerFusedProblem& p, cudaStream_t stream) 
 
 uint32_t take_zipformer_tc_error(cudaStream_t stream, bool clear, cudaError_t* err) {
     return take_error_word(g_zipformer_tc_error, stream, clear, err);
+}
+
+// Scratch of fga_zipformer_relative_attention_enqueue_no_workspace, for callers that cannot
+// allocate device memory: the weights kernel's work counter lives here instead of in a
+// caller-provided workspace. Every device that loads the library holds these bytes until
+// the process exits, and every call of that entry point on a device shares them, so two
+// such calls must not overlap on the GPU (the counter would be shared).
+static __device__ __align__(256) unsigned char g_no_workspace_scratch[FGA_NO_WORKSPACE_SCRATCH_BYTES];
+
+// Device address of the scratch on the current device. The name above is a host-side
+// stand-in, not a device address, so the address is looked up with cudaGetSymbolAddress,
+// once per device with that device current, and cached (devices past the cache are looked
+// up on every call).
+cudaError_t no_workspace_scratch(void** ptr) {
+    static std::atomic<void*> cache[kMaxCachedDevices];
+    const int dev = current_device();
+    if (dev < 0) return cudaErrorNoDevice;
+    if (dev < kMaxCachedDevices) {
+        if (void* p = cache[dev].load(std::memory_order_acquire)) {
+            *ptr = p;
+            return cudaSuccess;
+        }
+    }
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_no_workspace_scratch);
+    if (e != cudaSuccess) return e;
+    if (dev < kMaxCachedDevices) cache[dev].store(p, std::memory_order_release);
+    *ptr = p;
+    return cudaSuccess;
 }
 
 cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem& p, cudaStream_t stream) {

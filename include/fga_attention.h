@@ -134,6 +134,26 @@ FGA_API int32_t fga_zipformer_relative_attention_enqueue(const fga_tensor_desc* 
     const fga_tensor_desc* output_descs, const void* const* inputs, void* const* outputs,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference: a variant of fga_zipformer_relative_attention_enqueue
+ * for callers that cannot allocate device memory - code running where cudaMalloc is not
+ * permitted or not wanted (a fixed memory budget decided up front, an embedding host that
+ * hands out only input and output buffers, a binding with no device allocator) - and so
+ * cannot provide the FGA_SCHED_WORKSPACE_BYTES workspace. It takes no workspace and
+ * allocates nothing (no cudaMalloc, cudaFree or allocating library call): the kernel's
+ * work counter lives in a fixed device array of FGA_NO_WORKSPACE_SCRATCH_BYTES inside the
+ * library, which every GPU that loads the library holds until the process exits. A
+ * problem whose scratch needs exceed that array is rejected with FGA_ERROR_WORKSPACE.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress,
+ * with that device current); make that first call before any stream capture. Every call
+ * on a device shares the array: the counter is zeroed on the stream before each kernel,
+ * but calls that overlap on the GPU (different streams, concurrent graph replays) race
+ * on it and may produce wrong weights - order them, or use the workspace entry point.
+ * Same inputs, outputs, results and status codes as fga_zipformer_relative_attention_enqueue. */
+#define FGA_NO_WORKSPACE_SCRATCH_BYTES 256
+FGA_API int32_t fga_zipformer_relative_attention_enqueue_no_workspace(
+    const fga_tensor_desc* input_descs, const fga_tensor_desc* output_descs,
+    const void* const* inputs, void* const* outputs, void* stream);
+
 /* --------------------------------------------------------------------------------
  * zipformer_attention_value (apply shared attention weights to NTC values)
  *
