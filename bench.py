@@ -57,6 +57,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-gpu-reference", action="store_true",
+                   help="leave out the reference pipeline timed on this GPU")
     p.add_argument("--no-secondary", action="store_true",
                    help="default workload only: leave out the zipformer, parakeet_long and "
                         "zipformer_fused sub-lines")
@@ -682,7 +684,7 @@ def measure_workload(args, world, rank, local, peaks, *, with_e2e=True, with_cpu
     gpu_launches = args.steps * n_launch
 
     gpu_ref = None
-    if with_gpu_reference:
+    if with_gpu_reference and not args.no_gpu_reference:
         if is_parakeet(args):
             gpu_ref = gpu_reference_parakeet(layers, args, world, peaks, ms_per_step)
         else:

@@ -13,6 +13,9 @@ imports only the two attention modules, which need nothing but torch:
 * ``src/fast_gpu_asr/export/model/parakeet/attention.py``
   (``RelPositionMultiHeadAttention``, ``RelPositionalEncoding``)
 
+and, for ``positional_tables.npz``, the two positional encodings
+(``RelPositionalEncoding``, ``CompactRelPositionalEncoding``, zipformer/attention.py:292-374).
+
 Each fixture stores the plugin-boundary inputs (the projections the modules feed to
 their TensorRT plugins) and the module's eager output at that boundary. Output
 projections are set to (an embedding of) the identity so the module output equals
@@ -153,6 +156,20 @@ def parakeet_case(par_mod, name, dtype, n, t, heads, head_dim, seed, lengths, us
     print("wrote", name, tuple(out.shape))
 
 
+def positional_tables(zip_mod, par_mod) -> None:
+    """Row a7: the reference's positional tables, selected for sequence lengths shorter
+    than and equal to the table's maximum (the forward pass slices the central 2T-1 rows)."""
+    out = {}
+    for model_dim, max_len, t in ((1024, 50, 50), (64, 400, 375)):
+        enc = par_mod.RelPositionalEncoding(model_dim, max_len)
+        out[f"parakeet_{model_dim}_{t}"] = f32(enc(torch.zeros(1, t, model_dim)))
+    for embed_dim, max_len, t in ((48, 750, 750), (48, 800, 94)):
+        enc = zip_mod.CompactRelPositionalEncoding(embed_dim, max_len)
+        out[f"zipformer_{embed_dim}_{t}"] = f32(enc(torch.zeros(1, t, embed_dim)))
+    np.savez_compressed(HERE / "positional_tables.npz", **out)
+    print("wrote positional_tables", {k: v.shape for k, v in out.items()})
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", type=Path, required=True)
@@ -176,6 +193,7 @@ def main() -> None:
                   lengths=(44, 0))
     parakeet_case(par_mod, "parakeet_h1_d128_t160_fp16", "float16", 1, 160, 1, 128, seed=24,
                   lengths=(137,))
+    positional_tables(zip_mod, par_mod)
 
 
 if __name__ == "__main__":

@@ -19,7 +19,8 @@ from oracle import (
     zipformer_relative_attention,
 )
 
-GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz")
+                if p.stem.startswith(("zipformer_", "parakeet_")))
 
 
 @pytest.mark.parametrize("path", GOLDEN, ids=lambda p: p.stem)
@@ -170,3 +171,18 @@ def test_weight_check_accepts_only_ambiguous_content_rounding():
     wrong[0, 0, 0] = [0.6, 0.4]
     with pytest.raises(AssertionError):
         cases.assert_zipformer_weights_match(wrong, expected, proj, pos, mask, "bfloat16", heads)
+
+
+def test_positional_tables_match_the_reference_encoders():
+    """The positional tables that the workloads feed to linear_pos equal the reference's
+    RelPositionalEncoding (parakeet/attention.py:133-185) and CompactRelPositionalEncoding
+    (zipformer/attention.py:292-374), including when the reference's table is built for a
+    longer maximum and sliced (fixtures written by tests/golden/make_golden.py)."""
+    from fast_gpu_asr_b200.workloads import parakeet_positional_table, zipformer_positional_table
+
+    g = np.load(Path(__file__).parent / "golden" / "positional_tables.npz")
+    for key in g.files:
+        kind, dim, t = key.split("_")
+        ours = (parakeet_positional_table if kind == "parakeet" else zipformer_positional_table)(
+            int(dim), int(t))
+        np.testing.assert_allclose(ours.numpy()[None], g[key], rtol=0, atol=2e-6, err_msg=key)
