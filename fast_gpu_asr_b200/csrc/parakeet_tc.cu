@@ -126,22 +126,53 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// out[j] = v[j + s] for j < 64, s in [0, 31]: five predicated stages (16, 8, 4, 2, 1),
-// each touching only the entries the later stages still read. The coarse stages leave
-// entries 71..95 dead; the fine stages finish the shift.
-__device__ __forceinline__ void barrel_shift_coarse(uint32_t (&v)[96], uint32_t s) {
-#pragma unroll
-    for (int j = 0; j < 79; ++j) v[j] = (s & 16u) ? v[j + 16] : v[j];
-#pragma unroll
-    for (int j = 0; j < 71; ++j) v[j] = (s & 8u) ? v[j + 8] : v[j];
+// The positional band is held as packed pairs of the storage type T (element 2i in the
+// low half of word i): the reference's positional-score GEMM writes T as well
+// (parakeet_relative_attention_plugin.cu:1062-1087), and a 32-bit select then moves two
+// elements. out[e] = v[e + s] for e < 64, s in [0, 31]: four predicated word stages (8, 4,
+// 2 and 1 words = 16, 8, 4 and 2 elements), each touching only the words the later stages
+// still read, then one byte permute per word for an odd shift.
+template <typename T> __device__ __forceinline__ uint32_t pack_band(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack_band<__half>(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
+    return r;
 }
-__device__ __forceinline__ void barrel_shift_fine(uint32_t (&v)[96], uint32_t s) {
+template <> __device__ __forceinline__ uint32_t pack_band<__nv_bfloat16>(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void band_shift_words(uint32_t (&w)[48], uint32_t s) {
 #pragma unroll
-    for (int j = 0; j < 67; ++j) v[j] = (s & 4u) ? v[j + 4] : v[j];
+    for (int j = 0; j < 40; ++j) w[j] = (s & 16u) ? w[j + 8] : w[j];
 #pragma unroll
-    for (int j = 0; j < 65; ++j) v[j] = (s & 2u) ? v[j + 2] : v[j];
+    for (int j = 0; j < 36; ++j) w[j] = (s & 8u) ? w[j + 4] : w[j];
 #pragma unroll
-    for (int j = 0; j < 64; ++j) v[j] = (s & 1u) ? v[j + 1] : v[j];
+    for (int j = 0; j < 34; ++j) w[j] = (s & 4u) ? w[j + 2] : w[j];
+#pragma unroll
+    for (int j = 0; j < 33; ++j) w[j] = (s & 2u) ? w[j + 1] : w[j];
+}
+__device__ __forceinline__ void band_shift_odd(uint32_t (&w)[48], uint32_t s) {
+    // Selector 0x5432: the high element of word j and the low element of word j + 1.
+    const uint32_t sel = (s & 1u) ? 0x5432u : 0x3210u;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = __byte_perm(w[j], w[j + 1], sel);
+}
+
+// a + float(h) with the 16-bit value h of type T converted exactly (fma with 1.0).
+template <typename T> __device__ __forceinline__ float add_t16(float a, uint16_t h);
+template <> __device__ __forceinline__ float add_t16<__half>(float a, uint16_t h) {
+    float r;
+    asm("{\n\t.reg .b16 one;\n\tmov.b16 one, 0x3C00;\n\t"
+        "fma.rn.f32.f16 %0, %1, one, %2;\n\t}" : "=f"(r) : "h"(h), "f"(a));
+    return r;
+}
+template <> __device__ __forceinline__ float add_t16<__nv_bfloat16>(float a, uint16_t h) {
+    float r;
+    asm("{\n\t.reg .b16 one;\n\tmov.b16 one, 0x3F80;\n\t"
+        "fma.rn.f32.bf16 %0, %1, one, %2;\n\t}" : "=f"(r) : "h"(h), "f"(a));
+    return r;
 }
 
 // Maximum of 64 values with three-input max instructions (eight independent chains).
@@ -221,22 +252,27 @@ __device__ __forceinline__ uint32_t band_col(uint32_t x, uint32_t slot_lo) {
 // This thread's row of the tile as it sits in TMEM: the 96 band columns its 64 keys
 // reach (rows of a warp span 32 band columns, so the window is [base, base + 96) with
 // base = 96 - 32 group + 64 half, in three 32-column pieces that each lie inside one ring
-// slot), then S_c of those keys. The coarse shift stages run between the two loads so
-// that fewer values are live at once. Every load completes here, so the caller can
-// release S before the rest of the arithmetic and the next tile's score MMAs overlap
-// the skew and the exponentials.
-__device__ __forceinline__ void load_tile(uint32_t (&sc)[kHalfKeys], uint32_t (&band)[96],
+// slot), packed to T pairs, then S_c of those keys. The word shift stages run between
+// the two loads so that fewer values are live at once. Every load completes here, so the
+// caller can release S before the rest of the arithmetic and the next tile's score MMAs
+// overlap the skew and the exponentials.
+template <typename T>
+__device__ __forceinline__ void load_tile(uint32_t (&sc)[kHalfKeys], uint32_t (&band)[48],
                                           uint32_t tmem_row, int group, int half,
                                           uint32_t slot_lo, uint32_t shift) {
     const uint32_t base = 96u - 32u * group + 64u * half;
+    uint32_t raw[96];
 #pragma unroll
     for (int p = 0; p < 3; ++p)
         tmem_ld32(tmem_row + band_col(base + 32u * p, slot_lo),
-                  *reinterpret_cast<uint32_t(*)[32]>(band + 32 * p));
+                  *reinterpret_cast<uint32_t(*)[32]>(raw + 32 * p));
     tmem_wait_ld();
 #pragma unroll
-    for (int p = 0; p < 3; ++p) reg_fence(*reinterpret_cast<uint32_t(*)[32]>(band + 32 * p));
-    barrel_shift_coarse(band, shift);
+    for (int p = 0; p < 3; ++p) reg_fence(*reinterpret_cast<uint32_t(*)[32]>(raw + 32 * p));
+#pragma unroll
+    for (int i = 0; i < 48; ++i)
+        band[i] = pack_band<T>(__uint_as_float(raw[2 * i]), __uint_as_float(raw[2 * i + 1]));
+    band_shift_words(band, shift);
     tmem_ld64(tmem_row + kColSc + half * 64, sc);
     tmem_wait_ld();
     reg_fence(sc);
@@ -244,18 +280,18 @@ __device__ __forceinline__ void load_tile(uint32_t (&sc)[kHalfKeys], uint32_t (&
 
 // Unscaled logits S_c + band of this thread's 64 keys (row lane of its warp reads band
 // column base + key + 31 - lane); keys at or past the valid length are -inf.
-template <bool kMasked>
+template <typename T, bool kMasked>
 __device__ __forceinline__ void form_logits(float (&s)[kHalfKeys],
                                             const uint32_t (&sc)[kHalfKeys],
-                                            uint32_t (&band)[96], uint32_t shift, int nvalid) {
-    barrel_shift_fine(band, shift);
+                                            uint32_t (&band)[48], uint32_t shift, int nvalid) {
+    band_shift_odd(band, shift);
 #pragma unroll
     for (int e = 0; e < kHalfKeys; e += 2) {
-        const float2 v = f2_unpack(
-            f2_add(f2_pack(__uint_as_float(sc[e]), __uint_as_float(sc[e + 1])),
-                   f2_pack(__uint_as_float(band[e]), __uint_as_float(band[e + 1]))));
-        s[e] = (!kMasked || e < nvalid) ? v.x : -INFINITY;
-        s[e + 1] = (!kMasked || e + 1 < nvalid) ? v.y : -INFINITY;
+        const uint32_t w = band[e >> 1];
+        const float v0 = add_t16<T>(__uint_as_float(sc[e]), static_cast<uint16_t>(w & 0xFFFFu));
+        const float v1 = add_t16<T>(__uint_as_float(sc[e + 1]), static_cast<uint16_t>(w >> 16));
+        s[e] = (!kMasked || e < nvalid) ? v0 : -INFINITY;
+        s[e + 1] = (!kMasked || e + 1 < nvalid) ? v1 : -INFINITY;
     }
 }
 
@@ -616,16 +652,16 @@ parakeet_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                 const uint32_t slot_lo = (h_base + j) & 1;
                 float s[kHalfKeys];
                 {
-                    uint32_t sc[kHalfKeys], band[96];
-                    load_tile(sc, band, tmem_row, group, half, slot_lo, shift);
+                    uint32_t sc[kHalfKeys], band[48];
+                    load_tile<T>(sc, band, tmem_row, group, half, slot_lo, shift);
                     // Scores are in registers: the MMA warp may overwrite S with the next tile.
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sync.bar(kBarSFree));
                     if (nvalid >= kN)
-                        form_logits<false>(s, sc, band, shift, kHalfKeys);
+                        form_logits<T, false>(s, sc, band, shift, kHalfKeys);
                     else
-                        form_logits<true>(s, sc, band, shift, nvalid - half * kHalfKeys);
+                        form_logits<T, true>(s, sc, band, shift, nvalid - half * kHalfKeys);
                 }
 
                 const float m_half = tree_max(s);

@@ -703,25 +703,35 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             s[4 * t + 3] = fminf(s[4 * t + 3], m4.w);
                         }
                     }
-                    float gm = fmax3(s[0], s[1], s[2]);
+                    // Group max and sum as trees (four independent chains each), so the
+                    // dependent-instruction latency does not serialise the 32 keys.
+                    float m4[4];
 #pragma unroll
-                    for (int e = 3; e < 31; e += 2) gm = fmax3(gm, s[e], s[e + 1]);
-                    gm = fmaxf(gm, s[31]);
+                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(s[i], s[i + 4], s[i + 8]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[i + 12], s[i + 16]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[i + 20], s[i + 24]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) m4[i] = fmaxf(m4[i], s[i + 28]);
+                    const float gm = fmaxf(fmax3(m4[0], m4[1], m4[2]), m4[3]);
                     const float m_new = fmaxf(m_run, gm);
                     const float mb = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
                     const float2 nb = make_float2(-mb, -mb);
-                    float2 acc = make_float2(0.0f, 0.0f);
+                    float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                                     make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
                     uint32_t c16[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), l2e, nb);
                         const float e0 = fast_exp2(x.x), e1 = fast_exp2(x.y);
-                        acc = __fadd2_rn(acc, make_float2(e0, e1));
+                        acc[i & 3] = __fadd2_rn(acc[i & 3], make_float2(e0, e1));
                         c16[i] = pack_half2(e0, e1);
                     }
+                    const float2 accs = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
                     const float alpha =
                         m_run == m_new ? 1.0f : fast_exp2((m_run - m_new) * kLog2e);
-                    l_run = fmaf(l_run, alpha, acc.x + acc.y);
+                    l_run = fmaf(l_run, alpha, accs.x + accs.y);
                     m_run = m_new;
                     hist[g * kM + q_local] = m_new;
                     tmem_st16(tmem + lane_off + kCacheCol + g * (kGroup / 2), c16);
