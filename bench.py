@@ -54,6 +54,8 @@ def parse_args():
     p.add_argument("--batch", type=int, default=None,
                    help="utterances per GPU (default 256; 16 for parakeet_long)")
     p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--deal", choices=("longest_first", "round_robin"), default="longest_first",
+                   help="ragged workload: how batches are dealt to ranks")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -464,8 +466,9 @@ def workload_config(args) -> dict:
                 "l2": "per-layer inputs of distinct layers; head-0 weights up to 288 MB"}
     if args.workload == "ragged":
         return {"workload": "ragged whole-box run (config 5): 20,000 lognormal utterances, "
-                            "length-sorted batches of 256 dealt round-robin; per batch 24 "
-                            "parakeet layers (f16) + 19 zipformer layers (bf16)",
+                            f"length-sorted batches of 256 dealt {args.deal.replace('_', ' ')}; "
+                            "per batch 24 parakeet layers (f16) + 19 zipformer layers (bf16); "
+                            "outputs of both models gathered to rank 0",
                 "batch": args.batch, "utterances": 20000, "dtype": "f16+bf16",
                 "parallelism": f"dp{args.gpus}", "l2": "inputs exceed L2 for all but the "
                 "shortest batches; two input sets alternate per layer"}
@@ -477,8 +480,9 @@ def workload_config(args) -> dict:
 
 # ---- ragged whole-box run (config 5) -------------------------------------------------------
 def ragged_arm(args, world, rank, local):
-    """Length-sorted batches dealt round-robin; per batch the Parakeet stack (24 layers,
-    f16) and the Zipformer stacks (bf16); per-batch outputs gathered to rank 0 at the end.
+    """Length-sorted batches dealt to ranks (longest processing time first by default, or
+    round-robin); per batch the Parakeet stack (24 layers, f16) and the Zipformer stacks
+    (bf16); per-batch outputs of both models gathered to rank 0 at the end.
 
     ``value`` = audio seconds of all utterances / max over ranks of the summed kernel time
     (CUDA events around each batch's attention calls; inputs are generated on the device
@@ -489,18 +493,29 @@ def ragged_arm(args, world, rank, local):
     from fast_gpu_asr_b200 import _lib
     from fast_gpu_asr_b200 import workloads as wl
     from fast_gpu_asr_b200.attention import parakeet_relative_attention
-    from fast_gpu_asr_b200.sharding import gather_to_rank0, length_sorted_batches, shard_round_robin
+    from fast_gpu_asr_b200.sharding import (batch_costs, gather_to_rank0, length_sorted_batches,
+                                            shard_longest_first, shard_round_robin)
 
     _lib.library()
     stream = torch.cuda.Stream()
     durations = wl.ragged_durations()
     plan = length_sorted_batches(durations, args.batch)
-    mine = shard_round_robin(len(plan), world, rank)
-    kernel_ms, outputs, launches = 0.0, {}, 0
-    shapes = {}
+    if args.deal == "longest_first":
+        assignment = shard_longest_first(batch_costs(plan), world)
+    else:
+        assignment = [shard_round_robin(len(plan), world, r) for r in range(world)]
+    mine = assignment[rank]
+    kernel_ms, outputs, z_outputs, launches = 0.0, {}, {}, 0
+    shapes, z_shapes = {}, {}
     for b in plan:
         lens = np.maximum(1, np.floor(b.lengths / wl.PARAKEET_FRAME_SECONDS)).astype(np.int32)
         shapes[b.index] = (len(lens), int(lens.max()), 1024)
+        in_frames = np.maximum(2, np.round(b.lengths / wl.ZIPFORMER_INPUT_FRAME_SECONDS))
+        z_shapes[b.index] = []
+        for ds, _, embed, heads, _ in wl.ZIPFORMER_STACKS:
+            zt = int(wl.zipformer_stack_lengths(in_frames.astype(np.int64), ds).max())
+            z_shapes[b.index] += [(len(lens), zt, heads * wl.ZIPFORMER_VALUE_DIM),
+                                  (len(lens), zt, 3 * embed // 4)]
     for idx in mine:
         b = plan[idx]
         p_lens = np.maximum(1, np.floor(b.lengths / wl.PARAKEET_FRAME_SECONDS)).astype(np.int32)
@@ -532,24 +547,33 @@ def ragged_arm(args, world, rank, local):
         kernel_ms += start.elapsed_time(end)
         launches += wl.PARAKEET_LAYERS + 4 * sum(len(s[2]) for s in stacks)
         outputs[idx] = out
+        # The attention outputs of each stack's last layer (self-attention, nonlinear).
+        z_outputs[idx] = [t for s in stacks for t in s[3]]
         del players, stacks
     barrier(world)
     max_ms = allreduce_max(kernel_ms, world)
     rank_ms = allgather_floats(kernel_ms, world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    gathered = gather_to_rank0(outputs, shapes, world, rank, "cuda", torch.float16)
+    gathered = gather_to_rank0(outputs, shapes, world, rank, "cuda", torch.float16, assignment)
+    z_gathered = gather_to_rank0(z_outputs, z_shapes, world, rank, "cuda", torch.bfloat16,
+                                 assignment)
     torch.cuda.synchronize()
     gather_s = time.perf_counter() - t0
     if rank == 0:
         assert gathered is not None and len(gathered) == len(plan)
+        assert z_gathered is not None and len(z_gathered) == len(plan)
+        gathered_bytes = sum(t.numel() * t.element_size() for t in gathered.values()) + sum(
+            t.numel() * t.element_size() for ts in z_gathered.values() for t in ts)
         audio = float(durations.sum())
         line = {"metric": METRIC, "value": audio / (max_ms / 1000.0), "unit": UNIT,
                 "n_gpus": world, "steps": 1, "warmup": 0, "ms_per_step": max_ms,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f16+bf16", "data": "synthetic", "config": workload_config(args),
-                "batches": len(plan), "batches_per_rank": len(mine),
-                "rank_busy_ms": rank_ms, "gather_wall_s": gather_s, "gpu_launches": launches,
+                "batches": len(plan), "batches_per_rank": len(mine), "deal": args.deal,
+                "rank_busy_ms": rank_ms, "rank_busy_spread": max(rank_ms) / max(min(rank_ms), 1e-9),
+                "gather_wall_s": gather_s, "gathered_bytes": gathered_bytes,
+                "gpu_launches": launches,
                 "variant": _lib.last_kernel_variant()}
         print(json.dumps(line), flush=True)
 

@@ -8,8 +8,12 @@ benchmark configuration describes for the ragged whole-box run:
 
 * utterances are sorted by length and cut into batches of ``batch_size`` (similar lengths
   per batch keep the padded frame count low);
-* batch ``b`` goes to rank ``b % world`` (round-robin, so every rank gets a mix of long
-  and short batches);
+* batches are dealt to ranks either round-robin (batch ``b`` to rank ``b % world``) or,
+  by default in the ragged benchmark, longest processing time first: batches in order
+  of decreasing estimated cost, each to the rank with the least estimated work so far.
+  Round-robin over a length-sorted plan gives rank 0 the longest batch of every round,
+  which grows the slowest rank's share with the number of ranks; the greedy deal keeps
+  the estimated loads within one batch's cost of each other;
 * each rank runs its batches on its own GPU and stream;
 * at the end the per-batch outputs are gathered to rank 0 with point-to-point sends
   (NCCL over NVLink on GPUs, gloo in the CPU tests), outside the timed kernels.
@@ -54,37 +58,75 @@ def shard_round_robin(num_batches: int, world: int, rank: int) -> list[int]:
     return list(range(rank, num_batches, world))
 
 
+def batch_costs(plan: list[Batch]) -> np.ndarray:
+    """Estimated relative cost of each batch: utterances x (longest length)^2, the work of
+    attention over a batch padded to its longest utterance."""
+    return np.array([len(b.lengths) * float(b.max_length) ** 2 for b in plan])
+
+
+def shard_longest_first(costs, world: int) -> list[list[int]]:
+    """Longest-processing-time deal: batch indices per rank. Batches are taken in order of
+    decreasing cost (ties by index) and each goes to the rank with the least total cost so
+    far (ties to the lower rank). Deterministic, so every rank derives the same deal.
+    Each rank's list is in increasing batch order."""
+    if world < 1:
+        raise ValueError("world must be positive")
+    costs = np.asarray(costs, dtype=np.float64)
+    loads = np.zeros(world)
+    shards: list[list[int]] = [[] for _ in range(world)]
+    for b in sorted(range(len(costs)), key=lambda i: (-costs[i], i)):
+        r = int(np.argmin(loads))
+        shards[r].append(b)
+        loads[r] += costs[b]
+    return [sorted(s) for s in shards]
+
+
 def gather_to_rank0(outputs: dict, plan_shapes: dict, world: int, rank: int, device,
-                    dtype) -> dict | None:
+                    dtype, assignment: list[list[int]] | None = None) -> dict | None:
     """Gather every rank's per-batch outputs to rank 0.
 
-    ``outputs`` maps this rank's batch indices to tensors; ``plan_shapes`` maps every
-    batch index of the plan to its output shape (all ranks know the plan). Each rank sends
-    its batches' tensors, flattened in batch order, as one buffer; rank 0 receives the
-    buffers of the other ranks and returns {batch index: tensor} for the whole plan. The
-    other ranks return None. Collective: every rank must call it.
+    ``outputs`` maps this rank's batch indices to a tensor or a list of tensors;
+    ``plan_shapes`` maps every batch index of the plan to the shape, or list of shapes, of
+    those tensors (all ranks know the plan). ``assignment[r]`` lists rank r's batches
+    (default: round-robin). Each rank sends its batches' tensors, flattened in batch order,
+    as one buffer; rank 0 receives the buffers of the other ranks and returns {batch index:
+    tensor or list of tensors} for the whole plan. The other ranks return None.
+    Collective: every rank must call it. A rank that fails before its send makes rank 0's
+    receive fail (gloo: closed connection; NCCL: the process group's timeout) instead of
+    waiting for ever.
     """
     import torch
     import torch.distributed as dist
 
-    mine = shard_round_robin(len(plan_shapes), world, rank)
-    if sorted(outputs) != mine:
+    if assignment is None:
+        assignment = [shard_round_robin(len(plan_shapes), world, r) for r in range(world)]
+    mine = assignment[rank]
+    if sorted(outputs) != sorted(mine):
         raise ValueError("outputs must cover exactly this rank's batches")
+    single = {b: not isinstance(plan_shapes[b], list) for b in plan_shapes}
+    shapes = {b: [plan_shapes[b]] if single[b] else list(plan_shapes[b]) for b in plan_shapes}
     if world == 1:
         return dict(outputs)
+
+    def tensors(b):
+        return [outputs[b]] if single[b] else list(outputs[b])
+
     if rank != 0:
-        flat = (torch.cat([outputs[b].reshape(-1).to(dtype) for b in mine])
-                if mine else torch.empty(0, dtype=dtype, device=device))
+        parts = [t.reshape(-1).to(dtype) for b in mine for t in tensors(b)]
+        flat = torch.cat(parts) if parts else torch.empty(0, dtype=dtype, device=device)
         dist.send(flat.contiguous(), dst=0)
         return None
     gathered = dict(outputs)
     for src in range(1, world):
-        theirs = shard_round_robin(len(plan_shapes), world, src)
-        sizes = [int(np.prod(plan_shapes[b])) for b in theirs]
-        buf = torch.empty(sum(sizes), dtype=dtype, device=device)
+        theirs = assignment[src]
+        sizes = [[int(np.prod(sh)) for sh in shapes[b]] for b in theirs]
+        buf = torch.empty(sum(map(sum, sizes)), dtype=dtype, device=device)
         dist.recv(buf, src=src)
         off = 0
-        for b, n in zip(theirs, sizes):
-            gathered[b] = buf[off : off + n].reshape(plan_shapes[b])
-            off += n
+        for b, bsizes in zip(theirs, sizes):
+            got = []
+            for sh, n in zip(shapes[b], bsizes):
+                got.append(buf[off : off + n].reshape(sh))
+                off += n
+            gathered[b] = got[0] if single[b] else got
     return gathered

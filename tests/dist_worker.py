@@ -29,26 +29,54 @@ def batch_output(batch_index: int, batch_lengths: np.ndarray) -> np.ndarray:
     return zipformer_relative_attention(*batch_inputs(batch_index, batch_lengths))
 
 
-def run_rank(rank: int, world: int, port: int, lengths: list, batch_size: int, out_path: str):
+def run_rank(rank: int, world: int, port: int, lengths: list, batch_size: int, out_path: str,
+             deal: str = "round_robin", fail_rank: int = -1):
+    """One rank of the sharded run. ``deal``: "round_robin" or "longest_first" (then every
+    batch's output is a pair: the weights and their row sums, to exercise multi-tensor
+    gathers). ``fail_rank``: that rank raises after its compute, before the gather; rank 0
+    then records the error its gather raised in ``out_path`` + ".error"."""
     import torch
     import torch.distributed as dist
 
-    from fast_gpu_asr_b200.sharding import gather_to_rank0, length_sorted_batches, shard_round_robin
+    from fast_gpu_asr_b200.sharding import (batch_costs, gather_to_rank0, length_sorted_batches,
+                                            shard_longest_first, shard_round_robin)
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
     try:
         plan = length_sorted_batches(np.asarray(lengths), batch_size)
+        if deal == "longest_first":
+            assignment = shard_longest_first(batch_costs(plan), world)
+        else:
+            assignment = [shard_round_robin(len(plan), world, r) for r in range(world)]
         shapes = {}
         for b in plan:
             n, t = len(b.lengths), b.max_length
-            shapes[b.index] = (n, 2, t, t)
+            shapes[b.index] = (n, 2, t, t) if deal != "longest_first" else [(n, 2, t, t), (n, 2, t)]
         outputs = {}
-        for idx in shard_round_robin(len(plan), world, rank):
-            outputs[idx] = torch.from_numpy(batch_output(idx, plan[idx].lengths))
-        gathered = gather_to_rank0(outputs, shapes, world, rank, "cpu", torch.float32)
+        for idx in assignment[rank]:
+            w = torch.from_numpy(batch_output(idx, plan[idx].lengths))
+            outputs[idx] = w if deal != "longest_first" else [w, w.sum(dim=3)]
+        if rank == fail_rank:
+            raise RuntimeError(f"rank {rank} fails before the gather (injected)")
+        try:
+            gathered = gather_to_rank0(outputs, shapes, world, rank, "cpu", torch.float32,
+                                       assignment)
+        except Exception as e:  # noqa: BLE001 - recorded for the test
+            if rank == 0:
+                with open(out_path + ".error", "w") as f:
+                    f.write(f"{type(e).__name__}: {e}")
+            raise
         if rank == 0:
-            np.savez(out_path, **{str(k): v.numpy() for k, v in gathered.items()})
+            flat = {}
+            for k, v in gathered.items():
+                if isinstance(v, list):
+                    flat[f"{k}"] = v[0].numpy()
+                    flat[f"{k}_sum"] = v[1].numpy()
+                else:
+                    flat[str(k)] = v.numpy()
+            np.savez(out_path, **flat)
     finally:
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            dist.destroy_process_group()

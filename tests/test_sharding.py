@@ -7,7 +7,8 @@ import socket
 import numpy as np
 import pytest
 
-from fast_gpu_asr_b200.sharding import length_sorted_batches, shard_round_robin
+from fast_gpu_asr_b200.sharding import (batch_costs, length_sorted_batches,
+                                        shard_longest_first, shard_round_robin)
 from fast_gpu_asr_b200.workloads import ragged_durations
 
 
@@ -70,3 +71,65 @@ def test_gather_to_rank0_equals_single_process(tmp_path, world, count, batch):
     assert sorted(int(k) for k in got.files) == [b.index for b in plan]
     for b in plan:
         np.testing.assert_array_equal(got[str(b.index)], dist_worker.batch_output(b.index, b.lengths))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_longest_first_deal_balances_the_ragged_plan(world):
+    """On the ragged plan, the greedy deal keeps every rank within one batch's cost of the
+    others, and its slowest rank is no slower than round-robin's."""
+    plan = length_sorted_batches(ragged_durations(), 256)
+    costs = batch_costs(plan)
+    shards = shard_longest_first(costs, world)
+    assert sorted(b for s in shards for b in s) == list(range(len(plan)))
+    loads = [costs[s].sum() for s in shards]
+    assert max(loads) - min(loads) <= costs.max()
+    rr = [costs[shard_round_robin(len(plan), world, r)].sum() for r in range(world)]
+    assert max(loads) <= max(rr)
+    # Within 3 % of a perfect split, unless one batch alone is more than a rank's share.
+    assert max(loads) <= max(1.03 * costs.sum() / world, costs.max())
+    assert shard_longest_first(costs, world) == shards  # deterministic
+
+
+@pytest.mark.parametrize("world,count,batch", [(2, 23, 4), (3, 14, 3)])
+def test_gather_with_longest_first_deal_and_tensor_lists(tmp_path, world, count, batch):
+    import torch.multiprocessing as mp
+
+    import dist_worker
+
+    lengths = np.random.default_rng(10 + world).integers(3, 12, size=count).tolist()
+    out = tmp_path / "gathered.npz"
+    mp.start_processes(dist_worker.run_rank,
+                       args=(world, _free_port(), lengths, batch, str(out), "longest_first"),
+                       nprocs=world, join=True, start_method="spawn")
+    got = np.load(out)
+    plan = length_sorted_batches(np.asarray(lengths), batch)
+    for b in plan:
+        w = dist_worker.batch_output(b.index, b.lengths)
+        np.testing.assert_array_equal(got[str(b.index)], w)
+        np.testing.assert_allclose(got[f"{b.index}_sum"], w.sum(axis=3), rtol=1e-6)
+
+
+def test_rank_failing_before_the_gather_is_reported_not_hung(tmp_path):
+    """A rank that raises after its compute, before its send: rank 0's gather fails with an
+    error well within the process group's timeout (no hang), and it records the error."""
+    import time
+
+    import torch.multiprocessing as mp
+
+    import dist_worker
+
+    lengths = np.random.default_rng(3).integers(3, 12, size=12).tolist()
+    out = tmp_path / "gathered.npz"
+    ctx = mp.start_processes(dist_worker.run_rank,
+                             args=(2, _free_port(), lengths, 3, str(out), "round_robin", 1),
+                             nprocs=2, join=False, start_method="spawn")
+    t0 = time.monotonic()
+    for proc in ctx.processes:
+        proc.join(timeout=90)
+    elapsed = time.monotonic() - t0
+    assert all(not p.is_alive() for p in ctx.processes)
+    assert all(p.exitcode != 0 for p in ctx.processes)
+    assert elapsed < 60, elapsed
+    assert not out.exists()
+    err = (tmp_path / "gathered.npz.error").read_text()
+    assert err  # the receive from the failed rank raised on rank 0
