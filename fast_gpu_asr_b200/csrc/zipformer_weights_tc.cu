@@ -4,21 +4,23 @@
 // W[n, h, q, k] = softmax_k( round_T(Q[q] . K[k]) + sum_i pq[q,i] * pos[T-1-q+k, i] ),
 // masked keys excluded, written as the I/O dtype T in the NHTT layout.
 //
-// Launch shape: a persistent grid of one CTA per SM. A CTA takes (utterance, head) pairs
-// in a static stride and produces all query blocks (128 rows) of the pair, so Q and K of
+// Launch shape: a persistent grid of one CTA per SM. A CTA draws (utterance, head) pairs
+// from a work counter and produces all query blocks (128 rows) of the pair, so Q and K of
 // the head are loaded once per pair by TMA (SWIZZLE_64B, rows past T read as zero).
-// 8 compute warps (two per TMEM lane quarter) + 1 control warp that issues TMA and MMAs.
+// 16 compute warps (four per TMEM lane quarter; the fused variant: 8, two per quarter) + 1
+// control warp that issues TMA and MMAs.
 //
 // TMEM (512 columns, one CTA per SM):
 //   [0, 128)    two 64-key score buffers (content scores Q K^T, fp32), filled by the
 //               control warp, drained by the compute warps (mbarrier ring);
 //   [128, 512)  the row's exponentials as packed f16 pairs, key k at column 128 + k/2.
 //
-// Per query block (thread = query row, warp sub-slot = which 32 keys of each chunk):
+// Per query block (thread = query row, warp sub-slot = which kGroup keys of each chunk:
+// 16 in the weights kernel, 32 in the fused one):
 //   pass 1: logits -> group max -> exp2(logit - running max) in fp32, summed in fp32 and
 //           cached in TMEM as f16 (no logit is computed twice); the running max of every
-//           32-key group is kept in shared memory;
-//   combine the two sub-slots' (max, sum) per row;
+//           group is kept in shared memory;
+//   combine the sub-slots' (max, sum) per row;
 //   pass 2: cached exps x exp(group max - row max) / sum -> T, staged per warp in shared
 //           memory and written as 16-byte stores aligned to the global NHTT addresses
 //           (the row stride T*2 bytes is not 16-byte aligned for the encoder's lengths, so
@@ -57,12 +59,8 @@ constexpr int kQd = 32;             // query/key head dim served by this kernel
 constexpr int kMaxT = 768;          // keys held in shared memory / TMEM cache columns
 constexpr int kM = 128;             // query rows per block
 constexpr int kChunk = 64;          // keys per MMA (score buffer width)
-constexpr int kGroup = 32;          // keys per thread group
-constexpr int kMaxGroups = kMaxT / kGroup;
-constexpr int kSub = 2;             // compute warps per TMEM lane quarter
-constexpr int kComputeWarps = 4 * kSub;
-constexpr int kComputeThreads = 32 * kComputeWarps;
-constexpr int kThreads = kComputeThreads + 32;  // + control warp
+constexpr int kWord = 32;           // keys per key-validity word
+constexpr int kMaxWords = kMaxT / kWord;
 constexpr int kHalo = 7;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kCacheCol = 2 * kChunk;
@@ -77,51 +75,64 @@ constexpr int kPlane = 904;
 constexpr int kCopy = 4 * kPlane + 48;
 constexpr int kBandFill = kMaxT + kM + 4;  // band entries written per block
 
-// Pass 2 works in 64-key pieces. Per-warp staging tile: 32 rows x (16-byte carry chunk +
-// 64 keys), 144-byte rows (an odd number of 16-byte chunks, so row-parallel 16-byte
-// stores are bank-conflict free).
-constexpr int kPiece = 64;
-constexpr int kStageRow = 16 + kPiece * 2;
-constexpr int kStageWarp = 32 * kStageRow;
-
-// Dynamic pair scheduling: the CTAs draw pairs from one 32-bit counter in the caller's
-// workspace, which the launcher zeroes on the launch's stream just before the kernel.
-
 // Fused variant (weights applied to two value tensors in the same kernel): pass 2 writes
 // each 64-key piece of rounded weights into a P tile (one per warp sub-slot, 128 rows x
 // 64 keys, SWIZZLE_128B K-major) and the control warp multiplies it by the head's V
 // pieces, which stay resident for the whole pair (64 keys x 16 channels per piece,
 // SWIZZLE_32B MN-major, both value tensors).
-constexpr uint32_t kPTile = kM * kPiece * 2;
-constexpr uint32_t kVPiece = kPiece * 16 * 2;
+constexpr int kFusedPiece = 64;
+constexpr uint32_t kPTile = kM * kFusedPiece * 2;
+constexpr uint32_t kVPiece = kFusedPiece * 16 * 2;
 constexpr int kVBox = 256;  // keys per V TMA box (four pieces)
-constexpr uint32_t kVTensor = (kMaxT / kPiece) * kVPiece;
+constexpr uint32_t kVTensor = (kMaxT / kFusedPiece) * kVPiece;
 
-// Shared memory (bytes from the 1024-aligned base). The variant region holds the pass-2
-// staging tiles (weights kernel) or the P tiles and resident V (fused kernel).
-constexpr uint32_t kSmemQ = 0;
-constexpr uint32_t kSmemK = kSmemQ + kMaxT * kRowBytes;
-constexpr uint32_t kSmemBand = kSmemK + kMaxT * kRowBytes;
-constexpr uint32_t kSmemHist = kSmemBand + 4u * kCopy * 2u;
-constexpr uint32_t kSmemStats = kSmemHist + kMaxGroups * kM * 4;
-constexpr uint32_t kSmemKb = kSmemStats + kSub * kM * 8;          // 2 buffers (pair parity)
-constexpr uint32_t kSmemValid = kSmemKb + 2 * kMaxT * 4;           // 2 buffers
-constexpr uint32_t kSmemLive = kSmemValid + 2 * kMaxGroups * 4;    // 2 buffers x 8 words
-constexpr uint32_t kSmemVariant = (kSmemLive + 2 * 8 * 4 + 1023u) & ~1023u;
-constexpr uint32_t kSmemStage = kSmemVariant;
-constexpr uint32_t kSmemP = kSmemVariant;
-constexpr uint32_t kSmemV = kSmemP + kSub * kPTile;  // value v at + v * kVTensor
-template <bool kFused> struct SmemEnd {
+// Dynamic pair scheduling: the CTAs draw pairs from one 32-bit counter in the caller's
+// workspace, which the launcher zeroes on the launch's stream just before the kernel.
+
+// Work split and shared memory of each variant. kSub compute warps share a TMEM lane
+// quarter: in pass 1 each takes kGroup = 64 / kSub keys of every 64-key score chunk, in
+// pass 2 a contiguous range of kPiece-key pieces. The weights kernel runs four per quarter
+// (16 compute warps: enough warps in flight to hide the TMEM, shared-memory and MUFU
+// latencies of both passes) with 32-key pieces; the fused kernel two, with the 64-key
+// pieces of its P tiles.
+template <bool kFused> struct Cfg {
+    static constexpr int kSub = kFused ? 2 : 4;
+    static constexpr int kGroup = kChunk / kSub;  // keys per thread group
+    static constexpr int kMaxGroups = kMaxT / kGroup;
+    static constexpr int kComputeWarps = 4 * kSub;
+    static constexpr int kComputeThreads = 32 * kComputeWarps;
+    static constexpr int kThreads = kComputeThreads + 32;  // + control warp
+    // Pass 2 works in kPiece-key pieces. Per-warp staging tile: 32 rows x (16-byte carry
+    // chunk + kPiece keys), rows an odd number of 16-byte chunks long, so row-parallel
+    // 16-byte stores are bank-conflict free.
+    static constexpr int kPiece = kFused ? kFusedPiece : 32;
+    static constexpr int kStageRow = 16 + kPiece * 2;
+    static constexpr int kStageWarp = 32 * kStageRow;
+    // Shared memory (bytes from the 1024-aligned base). The variant region holds the
+    // pass-2 staging tiles (weights kernel) or the P tiles and resident V (fused kernel).
+    static constexpr uint32_t kSmemQ = 0;
+    static constexpr uint32_t kSmemK = kSmemQ + kMaxT * kRowBytes;
+    static constexpr uint32_t kSmemBand = kSmemK + kMaxT * kRowBytes;
+    static constexpr uint32_t kSmemHist = kSmemBand + 4u * kCopy * 2u;
+    static constexpr uint32_t kSmemStats = kSmemHist + kMaxGroups * kM * 4;
+    static constexpr uint32_t kSmemKb = kSmemStats + kSub * kM * 8;        // 2 buffers (pair parity)
+    static constexpr uint32_t kSmemValid = kSmemKb + 2 * kMaxT * 4;         // 2 buffers
+    static constexpr uint32_t kSmemLive = kSmemValid + 2 * kMaxWords * 4;   // 2 buffers x 8 words
+    static constexpr uint32_t kSmemVariant = (kSmemLive + 2 * 8 * 4 + 1023u) & ~1023u;
+    static constexpr uint32_t kSmemStage = kSmemVariant;
+    static constexpr uint32_t kSmemP = kSmemVariant;
+    static constexpr uint32_t kSmemV = kSmemP + kSub * kPTile;  // value v at + v * kVTensor
     // Barriers: [0, 64) shared by both variants; fused adds a_full[2], a_empty[2], v_full,
     // o_full, o_free at [64, 120).
     static constexpr uint32_t bar =
         kFused ? kSmemV + 2 * kVTensor : kSmemStage + kComputeWarps * kStageWarp + 16;
     static constexpr uint32_t bytes = bar + (kFused ? 128u : 64u);
+    static_assert(kStageRow % 32 == 16, "staging rows: an odd number of 16-byte chunks");
+    static_assert(kPiece == 2 * kGroup, "two thread groups per pass-2 piece");
+    static_assert(bytes <= 227 * 1024, "shared memory budget");
+    static_assert(kMaxT / kM <= kComputeWarps, "one warp per query block computes its liveness");
 };
 static_assert(kCopy % 64 == 16, "band copy stride");
-static_assert(SmemEnd<false>::bytes <= 227 * 1024 && SmemEnd<true>::bytes <= 227 * 1024,
-              "shared memory budget");
-static_assert(kMaxT / kM <= kComputeWarps, "one warp per query block computes its liveness");
 
 // Per-device error word of this file's kernels: 1 = a bounded wait gave up, 2 = the
 // dynamic shared memory was not 1024-byte aligned. Read and cleared by fga_device_status.
@@ -210,7 +221,8 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity,
 // the global addresses, as in pass 2 of the weights kernel.
 constexpr int kHalfStageRow = 16 + 32 * 2;
 constexpr int kHalfStageWarp = 32 * kHalfStageRow;
-static_assert(kComputeWarps * kHalfStageWarp + 16 <= 4 * kCopy * 2, "head-0 staging fits the band");
+static_assert(Cfg<true>::kComputeWarps * kHalfStageWarp + 16 <= 4 * kCopy * 2,
+              "head-0 staging fits the band");
 
 template <typename T>
 __device__ __forceinline__ void store_head0_half(T* __restrict__ out, uint8_t* stage_w,
@@ -268,7 +280,7 @@ __device__ __forceinline__ void store_head0_half(T* __restrict__ out, uint8_t* s
 // tensors [N, T, heads * vd] (v1_map, v2_map) into out1 and out2, and, when `out` is not
 // null, head 0's weights written as [N, 1, T, T].
 template <typename T, bool kFused>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<kFused>::kThreads, 1)
 zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             const __grid_constant__ CUtensorMap v1_map,
                             const __grid_constant__ CUtensorMap v2_map,
@@ -277,8 +289,19 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             T* __restrict__ out1, T* __restrict__ out2, int seq, int heads,
                             int vd, int num_pairs, unsigned int* __restrict__ sched,
                             uint64_t wait_limit) {
+    using C = Cfg<kFused>;
+    constexpr int kSub = C::kSub, kGroup = C::kGroup;
+    constexpr int kComputeWarps = C::kComputeWarps, kComputeThreads = C::kComputeThreads;
+    constexpr int kThreads = C::kThreads, kPiece = C::kPiece;
+    constexpr int kStageRow = C::kStageRow, kStageWarp = C::kStageWarp;
+    constexpr uint32_t kSmemQ = C::kSmemQ, kSmemK = C::kSmemK, kSmemBand = C::kSmemBand;
+    constexpr uint32_t kSmemHist = C::kSmemHist, kSmemStats = C::kSmemStats;
+    constexpr uint32_t kSmemKb = C::kSmemKb, kSmemValid = C::kSmemValid, kSmemLive = C::kSmemLive;
+    constexpr uint32_t kSmemStage = C::kSmemStage, kSmemP = C::kSmemP, kSmemV = C::kSmemV;
+    constexpr uint32_t kSmemBar = C::bar;
+    // Validity bits of a thread group's keys when all of them are valid.
+    constexpr uint32_t kGroupFull = kGroup == 32 ? 0xffffffffu : (1u << kGroup) - 1u;
     extern __shared__ __align__(1024) uint8_t smem[];
-    constexpr uint32_t kSmemBar = SmemEnd<kFused>::bar;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar_kq = sbase + kSmemBar;
     const uint32_t bar_full = sbase + kSmemBar + 8;   // + 8 * buffer
@@ -307,6 +330,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     const uint32_t lane_off = static_cast<uint32_t>(qtr * 32) << 16;
     const int pdim = heads * (2 * kQd + 4);
     const int ngroups = (seq + kGroup - 1) / kGroup;
+    const int nwords = (seq + kWord - 1) / kWord;
     const int nchunks = (seq + kChunk - 1) / kChunk;
     const int nqb = (seq + kM - 1) / kM;
     const int npieces = (seq + kPiece - 1) / kPiece;
@@ -388,17 +412,17 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
         const int buf = iter & 1;
         float* kb = reinterpret_cast<float*>(smem + kSmemKb) + buf * kMaxT;
-        uint32_t* valid = reinterpret_cast<uint32_t*>(smem + kSmemValid) + buf * kMaxGroups;
+        uint32_t* valid = reinterpret_cast<uint32_t*>(smem + kSmemValid) + buf * kMaxWords;
         uint32_t* live_q = reinterpret_cast<uint32_t*>(smem + kSmemLive) + buf * 8;
 
         if (!control) {
             // Key validity (bit per key, +-inf bias per key) and query-block liveness. Every
             // mask byte a thread needs is loaded before any is used (one memory round trip).
-            constexpr int kGroupIters = (kMaxGroups + kComputeWarps - 1) / kComputeWarps;
-            uint8_t mk[kGroupIters], mq[kM / 32];
+            constexpr int kWordIters = (kMaxWords + kComputeWarps - 1) / kComputeWarps;
+            uint8_t mk[kWordIters], mq[kM / 32];
 #pragma unroll
-            for (int i = 0; i < kGroupIters; ++i) {
-                const int k = (warp + i * kComputeWarps) * kGroup + lane;
+            for (int i = 0; i < kWordIters; ++i) {
+                const int k = (warp + i * kComputeWarps) * kWord + lane;
                 mk[i] = k < seq ? __ldg(mrow + k) : 1;
             }
 #pragma unroll
@@ -407,14 +431,14 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 mq[i] = (warp < nqb && q < seq && q >= kHalo) ? __ldg(mrow + q - kHalo) : 0;
             }
 #pragma unroll
-            for (int i = 0; i < kGroupIters; ++i) {
-                const int g = warp + i * kComputeWarps;
-                if (g < ngroups) {
-                    const int k = g * kGroup + lane;
+            for (int i = 0; i < kWordIters; ++i) {
+                const int wd = warp + i * kComputeWarps;
+                if (wd < nwords) {
+                    const int k = wd * kWord + lane;
                     const bool v = mk[i] == 0;
                     const uint32_t bits = __ballot_sync(0xffffffffu, v);
                     kb[k] = v ? INFINITY : -INFINITY;
-                    if (lane == 0) valid[g] = bits;
+                    if (lane == 0) valid[wd] = bits;
                 }
             }
             if (warp < nqb) {
@@ -435,7 +459,13 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
         named_barrier(1, kThreads);  // mask information of this pair is visible
 
         bool any_valid = false;
-        for (int g = 0; g < ngroups; ++g) any_valid |= valid[g] != 0u;
+        for (int wd = 0; wd < nwords; ++wd) any_valid |= valid[wd] != 0u;
+        // Validity bits of the keys of thread group g (g < ngroups).
+        auto group_bits = [&](int g) -> uint32_t {
+            if constexpr (kGroup == kWord) return valid[g];
+            else return (valid[g / (kWord / kGroup)] >> ((g % (kWord / kGroup)) * kGroup)) &
+                        kGroupFull;
+        };
         uint32_t live_mask = 0;
         for (int b = 0; b < nqb; ++b)
             if (any_valid && live_q[b] != 0u) live_mask |= 1u << b;
@@ -590,7 +620,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             if (block_live) {
                 named_barrier(2, kComputeThreads);  // previous block's band/cache readers done
                 // Positional band of this block: entry i is relative row T-1-q0-127+i. Pass 1
-                // reads entries below 127 + 32 * ngroups.
+                // reads entries below 127 + kGroup * ngroups.
                 const int band_lo = seq - 1 - q0 - (kM - 1);
                 const int band_fill = min(kBandFill, kM + ngroups * kGroup + 4);
                 // All of this thread's positional rows and its query's positional
@@ -652,13 +682,13 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 for (int j = 0; j < nchunks; ++j) {
                     const uint32_t u = ucount + j;
                     const uint32_t sb = u & 1;
-                    const int g = 2 * j + sub;
-                    const uint32_t vb = g < ngroups ? valid[g] : 0u;
+                    const int g = kSub * j + sub;
+                    const uint32_t vb = g < ngroups ? group_bits(g) : 0u;
                     const bool math = warp_live && vb != 0u;
                     const bool ok = warp_wait(bar_full + 8 * sb, (u >> 1) & 1, abort, wait_limit);
-                    uint32_t r[32];
+                    uint32_t r[kGroup];
                     if (ok && math) {
-                        tmem_ld32(tmem + lane_off + sb * kChunk + sub * kGroup, r);
+                        tmem_ld_cols(tmem + lane_off + sb * kChunk + sub * kGroup, r);
                         tmem_wait_ld();
                         reg_fence(r);
                     }
@@ -669,9 +699,9 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                         if (g < ngroups) hist[g * kM + q_local] = -INFINITY;
                         continue;
                     }
-                    float s[32];
+                    float s[kGroup];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
+                    for (int i = 0; i < kGroup / 2; ++i) {
                         const float2 f = round_pair<T>(__uint_as_float(r[2 * i]),
                                                        __uint_as_float(r[2 * i + 1]));
                         s[2 * i] = f.x;
@@ -682,7 +712,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     const int cpy = b0 & 3;
                     const uint16_t* bp = band + cpy * kCopy + (b0 - cpy);
 #pragma unroll
-                    for (int t = 0; t < 8; ++t) {
+                    for (int t = 0; t < kGroup / 4; ++t) {
 #pragma unroll
                         for (int pl = 0; pl < 4; ++pl) {
                             const uint2 v = *reinterpret_cast<const uint2*>(bp + pl * kPlane + 4 * t);
@@ -690,12 +720,12 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                             fma_pair<T>(s[4 * t + 2], s[4 * t + 3], pq[pl], v.y);
                         }
                     }
-                    if (vb != 0xffffffffu) {
+                    if (vb != kGroupFull) {
                         // Some keys of the group are masked or past T: min with -inf
                         // removes them whatever their score (NaN included).
                         const float* kp = kb + g * kGroup;
 #pragma unroll
-                        for (int t = 0; t < 8; ++t) {
+                        for (int t = 0; t < kGroup / 4; ++t) {
                             const float4 m4 = *reinterpret_cast<const float4*>(kp + 4 * t);
                             s[4 * t] = fminf(s[4 * t], m4.x);
                             s[4 * t + 1] = fminf(s[4 * t + 1], m4.y);
@@ -704,25 +734,28 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                         }
                     }
                     // Group max and sum as trees (four independent chains each), so the
-                    // dependent-instruction latency does not serialise the 32 keys.
+                    // dependent-instruction latency does not serialise the group's keys.
                     float m4[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(s[i], s[i + 4], s[i + 8]);
+                    for (int i = 0; i < 4; ++i) m4[i] = s[i];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[i + 12], s[i + 16]);
+                    for (int t = 1; t + 1 < kGroup / 4; t += 2) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[i + 20], s[i + 24]);
+                        for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[i + 4 * t], s[i + 4 * t + 4]);
+                    }
+                    if constexpr ((kGroup / 4) % 2 == 0) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) m4[i] = fmaxf(m4[i], s[i + 28]);
+                        for (int i = 0; i < 4; ++i) m4[i] = fmaxf(m4[i], s[i + kGroup - 4]);
+                    }
                     const float gm = fmaxf(fmax3(m4[0], m4[1], m4[2]), m4[3]);
                     const float m_new = fmaxf(m_run, gm);
                     const float mb = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
                     const float2 nb = make_float2(-mb, -mb);
                     float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
                                      make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-                    uint32_t c16[16];
+                    uint32_t c16[kGroup / 2];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
+                    for (int i = 0; i < kGroup / 2; ++i) {
                         const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), l2e, nb);
                         const float e0 = fast_exp2(x.x), e1 = fast_exp2(x.y);
                         acc[i & 3] = __fadd2_rn(acc[i & 3], make_float2(e0, e1));
@@ -734,7 +767,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     l_run = fmaf(l_run, alpha, accs.x + accs.y);
                     m_run = m_new;
                     hist[g * kM + q_local] = m_new;
-                    tmem_st16(tmem + lane_off + kCacheCol + g * (kGroup / 2), c16);
+                    tmem_st_cols(tmem + lane_off + kCacheCol + g * (kGroup / 2), c16);
                 }
                 ucount += nchunks;
                 tmem_wait_st();
@@ -793,8 +826,8 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             const bool all_live = __all_sync(0xffffffffu, row_live);
             const bool use_tmem = block_live && __any_sync(0xffffffffu, row_live) &&
                                   __all_sync(0xffffffffu, *abort == 0u);
-            const int p_lo = sub == 0 ? 0 : split;
-            const int p_hi = sub == 0 ? split : npieces;
+            const int p_lo = (sub * npieces + kSub - 1) / kSub;
+            const int p_hi = ((sub + 1) * npieces + kSub - 1) / kSub;
             const int kb_w = p_lo * kPiece;
             const int ke_w = min(p_hi * kPiece, seq);
             const int rows_here = min(32, seq - (q0 + qtr * 32));
@@ -802,18 +835,19 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 (static_cast<int64_t>(n * heads + h) * seq + q0 + qtr * 32) * seq;
             uint8_t* stage_w = smem + kSmemStage + warp * kStageWarp;
             uint8_t* srow = stage_w + lane * kStageRow;
-            auto group_valid = [&](int g) { return g < ngroups && valid[g] != 0u; };
+            auto group_valid = [&](int g) { return g < ngroups && group_bits(g) != 0u; };
             auto piece_cached = [&](int pc) {
                 return use_tmem && (group_valid(2 * pc) || group_valid(2 * pc + 1));
             };
-            uint32_t c[32];
+            constexpr int kGw = kGroup / 2;  // cache words (f16 pairs) of a thread group
+            uint32_t c[kPiece / 2];
             if (p_lo < p_hi && piece_cached(p_lo))
-                tmem_ld32(tmem + lane_off + kCacheCol + p_lo * (kPiece / 2), c);
+                tmem_ld_cols(tmem + lane_off + kCacheCol + p_lo * (kPiece / 2), c);
             uint4 carry = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll 1
             for (int pc = p_lo; pc < p_hi; ++pc) {
                 const int k0 = pc * kPiece;
-                uint32_t w[32];
+                uint32_t w[kPiece / 2];
                 if (piece_cached(pc)) {
                     tmem_wait_ld();
                     reg_fence(c);
@@ -826,27 +860,27 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                                 row_live ? fast_exp2((hm - m_fin) * kLog2e) * inv : 0.0f;
                             const float2 sc = make_float2(scale, scale);
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                const float2 f = __fmul2_rn(unpack_half2(c[16 * half + i]), sc);
-                                w[16 * half + i] = pack_pair<T>(f.x, f.y);
+                            for (int i = 0; i < kGw; ++i) {
+                                const float2 f = __fmul2_rn(unpack_half2(c[kGw * half + i]), sc);
+                                w[kGw * half + i] = pack_pair<T>(f.x, f.y);
                             }
                             if (!all_live) {
 #pragma unroll
-                                for (int i = 0; i < 16; ++i)
-                                    w[16 * half + i] = row_live ? w[16 * half + i] : 0u;
+                                for (int i = 0; i < kGw; ++i)
+                                    w[kGw * half + i] = row_live ? w[kGw * half + i] : 0u;
                             }
                         } else {
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) w[16 * half + i] = 0u;
+                            for (int i = 0; i < kGw; ++i) w[kGw * half + i] = 0u;
                         }
                     }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) w[i] = 0u;
+                    for (int i = 0; i < kPiece / 2; ++i) w[i] = 0u;
                 }
                 // Next piece's exps are read from TMEM while this one is written out.
                 if (pc + 1 < p_hi && piece_cached(pc + 1))
-                    tmem_ld32(tmem + lane_off + kCacheCol + (pc + 1) * (kPiece / 2), c);
+                    tmem_ld_cols(tmem + lane_off + kCacheCol + (pc + 1) * (kPiece / 2), c);
                 if constexpr (kFused) {
                     // The piece's rounded weights go to this sub-slot's P tile (row q_local,
                     // keys k0..k0+63) once the control warp's previous P.V has read it.
@@ -872,18 +906,21 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 }
                 *reinterpret_cast<uint4*>(srow) = carry;
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
+                for (int i = 0; i < kPiece / 8; ++i)
                     *reinterpret_cast<uint4*>(srow + 16 + 16 * i) =
                         make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-                carry = make_uint4(w[28], w[29], w[30], w[31]);
+                carry = make_uint4(w[kPiece / 2 - 4], w[kPiece / 2 - 3], w[kPiece / 2 - 2],
+                                   w[kPiece / 2 - 1]);
                 __syncwarp();
                 // Staging element i of a row holds key k0 - 8 + i. A slot is an 8-element
                 // run whose start is 16-byte aligned in the output; slot m of this piece
-                // starts at key k0 - d + 8m, d = (row's element offset) mod 8.
+                // starts at key k0 - d + 8m, d = (row's element offset) mod 8. Each lane
+                // writes one slot; kSlots lanes cover a row.
+                constexpr int kSlots = kPiece / 8;
 #pragma unroll
-                for (int it = 0; it < 8; ++it) {
-                    const int row = it * 4 + (lane >> 3);
-                    const int m = lane & 7;
+                for (int it = 0; it < kSlots; ++it) {
+                    const int row = it * (32 / kSlots) + lane / kSlots;
+                    const int m = lane % kSlots;
                     if (row < rows_here) {
                         const int64_t e_row = e_base + static_cast<int64_t>(row) * seq;
                         const int d = static_cast<int>(e_row & 7);
@@ -905,7 +942,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     }
                 }
                 if (pc + 1 == p_hi && lane < rows_here) {
-                    // Keys after the last slot of the range (slot m = 8, always partial).
+                    // Keys after the last slot of the range (slot m = kSlots, always partial).
                     const int64_t e_row = e_base + static_cast<int64_t>(lane) * seq;
                     const int d = static_cast<int>(e_row & 7);
                     const int lo = k0 - d + kPiece;
@@ -1012,7 +1049,7 @@ template <typename T, bool kFused>
 cudaError_t set_smem_attr() {
     static SmemAttr attr;
     return attr.ensure(reinterpret_cast<const void*>(zipformer_weights_tc_kernel<T, kFused>),
-                       static_cast<int>(SmemEnd<kFused>::bytes));
+                       static_cast<int>(Cfg<kFused>::bytes));
 }
 
 // The work counter starts at zero for every launch: a 4-byte memset on the same stream,
@@ -1034,7 +1071,7 @@ cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stre
     if (sms <= 0) return cudaErrorNotSupported;
     const int grid = static_cast<int>(pairs < sms ? pairs : sms);
     if (cudaError_t e = zero_counter(p.sched, stream); e != cudaSuccess) return e;
-    zipformer_weights_tc_kernel<T, false><<<grid, kThreads, SmemEnd<false>::bytes, stream>>>(
+    zipformer_weights_tc_kernel<T, false><<<grid, Cfg<false>::kThreads, Cfg<false>::bytes, stream>>>(
         map, unused, unused, static_cast<const T*>(p.projection),
         static_cast<const T*>(p.position), p.mask, static_cast<T*>(p.weights), nullptr, nullptr,
         p.length, p.heads, 0, static_cast<int>(pairs), p.sched, wait_limit_ns());
@@ -1057,7 +1094,7 @@ cudaError_t fused_tc_typed(const ZipformerFusedProblem& p, cudaStream_t stream) 
     if (sms <= 0) return cudaErrorNotSupported;
     const int grid = static_cast<int>(pairs < sms ? pairs : sms);
     if (cudaError_t e = zero_counter(p.sched, stream); e != cudaSuccess) return e;
-    zipformer_weights_tc_kernel<T, true><<<grid, kThreads, SmemEnd<true>::bytes, stream>>>(
+    zipformer_weights_tc_kernel<T, true><<<grid, Cfg<true>::kThreads, Cfg<true>::bytes, stream>>>(
         map, v1, v2, static_cast<const T*>(p.projection), static_cast<const T*>(p.position),
         p.mask, static_cast<T*>(p.weights0), static_cast<T*>(p.output1),
         static_cast<T*>(p.output2), p.length, p.heads, p.value_dim, static_cast<int>(pairs),

@@ -143,10 +143,15 @@ def test_zipformer_config3_every_utterance(stack):
 
 @pytest.mark.parametrize("stack", [0, 1, 3], ids=["stack1", "stack2", "stack4"])
 def test_zipformer_fused_config3_every_utterance(stack):
-    """The fused entry point on a full-size layer, every utterance: head 0's weights are
-    bit-identical to the weights entry point's, and both SelfAttention outputs match the
-    attention-value entry point applied to those weights (checked against the oracle by
-    test_zipformer_config3_every_utterance)."""
+    """The fused entry point on a full-size layer, every utterance: head 0's weights agree
+    with the weights entry point's, and both SelfAttention outputs match the attention-value
+    entry point applied to those weights (checked against the oracle by
+    test_zipformer_config3_every_utterance).
+
+    The two kernels split a row's keys into different groups (32 and 16 keys per thread),
+    so their f16 exponential caches hold values relative to different running maxima and
+    a weight may round to the neighbouring bf16 value in one of them: head 0 agrees within
+    the weight tolerance against each other's value (1e-3 plus one ulp)."""
     layer, heads = zipformer_stack_layer(stack)
     o1, o2, w0 = zipformer_attention_fused(layer.projection, layer.position, layer.mask,
                                            layer.value_a, layer.value_b)
@@ -154,7 +159,9 @@ def test_zipformer_fused_config3_every_utterance(stack):
     r1 = zipformer_attention_value(w, layer.value_a, heads)
     r2 = zipformer_attention_value(w, layer.value_b, heads)
     torch.cuda.synchronize()
-    assert torch.equal(w0, w[:, :1])
+    a, b = cpu(w0), cpu(w[:, :1])
+    close = cases.weights_within_tolerance(a, b, "bfloat16")
+    assert close.all(), (int((~close).sum()), float(np.abs(a - b).max()))
     for o, r in ((o1, r1), (o2, r2)):
         diff = (o.float() - r.float()).abs().max().item()
         assert diff <= cases.PARAKEET_TOL["bfloat16"], diff
