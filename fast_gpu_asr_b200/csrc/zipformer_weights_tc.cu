@@ -844,6 +844,30 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
             if (p_lo < p_hi && piece_cached(p_lo))
                 tmem_ld_cols(tmem + lane_off + kCacheCol + p_lo * (kPiece / 2), c);
             uint4 carry = make_uint4(0u, 0u, 0u, 0u);
+            // Staging element i of a row holds key k0 - 8 + i. A slot is an 8-element run
+            // whose start is 16-byte aligned in the output; slot m of a piece starts at key
+            // k0 - d + 8m, d = (row's element offset) mod 8. Each lane writes one slot of
+            // kRowSlots rows (kRowSlots lanes cover a row). What a lane's slots need that
+            // does not change from piece to piece is computed once per block: the slot's
+            // element offset from the block's first output element at piece 0, the
+            // staging word it starts in and the byte selector of its re-alignment.
+            constexpr int kRowSlots = kPiece / 8;
+            int slot_off[kRowSlots];
+            uint32_t slot_word[kRowSlots], slot_sel[kRowSlots];
+            uint32_t slot_live = 0;
+            if constexpr (!kFused) {
+#pragma unroll
+                for (int it = 0; it < kRowSlots; ++it) {
+                    const int row = it * (32 / kRowSlots) + lane / kRowSlots;
+                    const int m = lane % kRowSlots;
+                    const int d = static_cast<int>((e_base + static_cast<int64_t>(row) * seq) & 7);
+                    const int s0 = 8 - d + 8 * m;
+                    slot_off[it] = row * seq - d + 8 * m;
+                    slot_word[it] = static_cast<uint32_t>(row * kStageRow) / 4u + (s0 >> 1);
+                    slot_sel[it] = (s0 & 1) ? 0x5432u : 0x3210u;
+                    if (row < rows_here) slot_live |= 1u << it;
+                }
+            }
 #pragma unroll 1
             for (int pc = p_lo; pc < p_hi; ++pc) {
                 const int k0 = pc * kPiece;
@@ -912,15 +936,28 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                 carry = make_uint4(w[kPiece / 2 - 4], w[kPiece / 2 - 3], w[kPiece / 2 - 2],
                                    w[kPiece / 2 - 1]);
                 __syncwarp();
-                // Staging element i of a row holds key k0 - 8 + i. A slot is an 8-element
-                // run whose start is 16-byte aligned in the output; slot m of this piece
-                // starts at key k0 - d + 8m, d = (row's element offset) mod 8. Each lane
-                // writes one slot; kSlots lanes cover a row.
-                constexpr int kSlots = kPiece / 8;
+                if (pc > p_lo && pc + 1 < p_hi) {
+                    // An inner piece of the range: every slot lies inside [kb_w, ke_w).
+                    const uint32_t* sw = reinterpret_cast<const uint32_t*>(stage_w);
+                    T* const ob = out + e_base + k0;
 #pragma unroll
-                for (int it = 0; it < kSlots; ++it) {
-                    const int row = it * (32 / kSlots) + lane / kSlots;
-                    const int m = lane % kSlots;
+                    for (int it = 0; it < kRowSlots; ++it) {
+                        if ((slot_live >> it) & 1u) {
+                            const uint32_t* wp = sw + slot_word[it];
+                            const uint32_t a0 = wp[0], a1 = wp[1], a2 = wp[2], a3 = wp[3], a4 = wp[4];
+                            const uint32_t sel = slot_sel[it];
+                            *reinterpret_cast<uint4*>(ob + slot_off[it]) =
+                                make_uint4(__byte_perm(a0, a1, sel), __byte_perm(a1, a2, sel),
+                                           __byte_perm(a2, a3, sel), __byte_perm(a3, a4, sel));
+                        }
+                    }
+                    __syncwarp();
+                    continue;
+                }
+#pragma unroll
+                for (int it = 0; it < kRowSlots; ++it) {
+                    const int row = it * (32 / kRowSlots) + lane / kRowSlots;
+                    const int m = lane % kRowSlots;
                     if (row < rows_here) {
                         const int64_t e_row = e_base + static_cast<int64_t>(row) * seq;
                         const int d = static_cast<int>(e_row & 7);
@@ -942,7 +979,7 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
                     }
                 }
                 if (pc + 1 == p_hi && lane < rows_here) {
-                    // Keys after the last slot of the range (slot m = kSlots, always partial).
+                    // Keys after the last slot of the range (slot m = kRowSlots, always partial).
                     const int64_t e_row = e_base + static_cast<int64_t>(lane) * seq;
                     const int d = static_cast<int>(e_row & 7);
                     const int lo = k0 - d + kPiece;
