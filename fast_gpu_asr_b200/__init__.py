@@ -2,9 +2,10 @@
 
 Drop-in replacement for the reference's three attention TensorRT plugins
 (``parakeet_relative_attention``, ``zipformer_relative_attention``,
-``zipformer_attention_value``): hand-written CUDA kernels behind the C ABI in
-``include/fga_attention.h``, the same plugin identities for TensorRT, and a
-data-parallel batch-sharding launcher.
+``zipformer_attention_value``) and its two convolution-module plugins
+(``parakeet_conformer_convolution``, ``zipformer_convolution``): hand-written CUDA
+kernels behind the C ABI in ``include/fga_attention.h`` and ``include/fga_convolution.h``,
+the same plugin identities for TensorRT, and a data-parallel batch-sharding launcher.
 """
 
 from .attention import (  # noqa: F401
@@ -13,11 +14,17 @@ from .attention import (  # noqa: F401
     zipformer_attention_value,
     zipformer_relative_attention,
 )
+from .convolution import (  # noqa: F401
+    parakeet_conformer_convolution,
+    zipformer_convolution,
+)
 from .constants import (  # noqa: F401
+    PARAKEET_CONFORMER_CONVOLUTION_PLUGIN_NAME,
     PARAKEET_RELATIVE_ATTENTION_PLUGIN_NAME,
     PLUGIN_VERSION,
     TENSORRT_PLUGIN_NAMESPACE,
     ZIPFORMER_ATTENTION_VALUE_PLUGIN_NAME,
+    ZIPFORMER_CONVOLUTION_PLUGIN_NAME,
     ZIPFORMER_RELATIVE_ATTENTION_PLUGIN_NAME,
 )
 

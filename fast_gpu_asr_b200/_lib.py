@@ -36,6 +36,7 @@ STATUS_NAMES = {
     10: "FGA_ERROR_WORKSPACE",
     11: "FGA_ERROR_DEVICE_ABORT",
 }
+STATUS_CODES = {name: code for code, name in STATUS_NAMES.items()}
 
 
 class TensorDesc(ctypes.Structure):
@@ -91,6 +92,18 @@ SYMBOLS = {
         ctypes.c_int32, (_P, ctypes.c_int32, _P, ctypes.c_int32)),
     "fga_zipformer_attention_fused_workspace_size": (ctypes.c_size_t, (_P, ctypes.c_int32)),
     "fga_zipformer_attention_fused_enqueue": (
+        ctypes.c_int32,
+        (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP, ctypes.c_size_t, _VP)),
+    "fga_parakeet_conformer_convolution_check": (
+        ctypes.c_int32, (_P, ctypes.c_int32, _P, ctypes.c_int32)),
+    "fga_parakeet_conformer_convolution_workspace_size": (ctypes.c_size_t, (_P, ctypes.c_int32)),
+    "fga_parakeet_conformer_convolution_enqueue": (
+        ctypes.c_int32,
+        (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP, ctypes.c_size_t, _VP)),
+    "fga_zipformer_convolution_check": (
+        ctypes.c_int32, (_P, ctypes.c_int32, _P, ctypes.c_int32)),
+    "fga_zipformer_convolution_workspace_size": (ctypes.c_size_t, (_P, ctypes.c_int32)),
+    "fga_zipformer_convolution_enqueue": (
         ctypes.c_int32,
         (_P, _P, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _VP, ctypes.c_size_t, _VP)),
     "fga_abi_version": (ctypes.c_int32, ()),

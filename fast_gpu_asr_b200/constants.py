@@ -11,6 +11,8 @@ PLUGIN_VERSION = "1"
 PARAKEET_RELATIVE_ATTENTION_PLUGIN_NAME = "parakeet_relative_attention"
 ZIPFORMER_RELATIVE_ATTENTION_PLUGIN_NAME = "zipformer_relative_attention"
 ZIPFORMER_ATTENTION_VALUE_PLUGIN_NAME = "zipformer_attention_value"
+PARAKEET_CONFORMER_CONVOLUTION_PLUGIN_NAME = "parakeet_conformer_convolution"
+ZIPFORMER_CONVOLUTION_PLUGIN_NAME = "zipformer_convolution"
 
 # zipformer_relative_attention_plugin.cu:41-42
 ZIPFORMER_POSITION_HEAD_DIM = 4

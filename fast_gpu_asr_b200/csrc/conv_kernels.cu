@@ -1,0 +1,299 @@
+// Depthwise temporal convolution of the encoders' convolution modules, NTC storage:
+//   parakeet_conformer_convolution: masked depthwise convolution with the evaluation-mode
+//     BatchNorm folded into weight and bias, then SiLU;
+//   zipformer_convolution: masked depthwise convolution, then Swoosh-R.
+//
+//   y[n,t,c] = act( bias[c] + sum_k w[k,c] * xm[n, t+k-K/2, c] )
+//
+// xm is x on the frames below the utterance's valid length (clamped to [0, T]) and zero
+// elsewhere; output frames past the valid length are written too (not re-masked).
+//
+// Reference semantics (parakeet_convolution_plugin.cu:105-157, 241-352, 598-623;
+// zipformer_convolution_plugin.cu:104-109, 156-199, 275-509, 790-835):
+// - f16/bf16 accumulate in the storage type: starting from the bias, one packed fused
+//   multiply-add per tap in tap order, each rounding to the storage type; the activation
+//   is evaluated in fp32 on the rounded sum and rounded once at the store. fp32 uses one
+//   fmaf per tap in the same order.
+// - A tap on a padded or out-of-range frame is a multiply-add with a zero input, except
+//   in the Parakeet paths that skip it (fp32, and f16/bf16 when C % 8 != 0). The two differ
+//   only for non-finite weights or a -0 sum; this library takes the same path as the
+//   reference for every (dtype, C).
+//
+// Launch shape: a warp computes kFrames consecutive output frames x 64 channels of one
+// utterance; lane l holds channel pair l of the slab, so each frame is read and written as
+// one coalesced 128-byte row (16-bit types). Each input frame is loaded once per tile and
+// applied to every output frame of the tile it reaches. Warps take equal contiguous runs
+// of the tiles ordered (channel slab, utterance, frame tile): a warp reloads weights only
+// when its slab changes, and a tile's halo frames are mostly the previous tile's, still in
+// L1.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <atomic>
+#include <cstdint>
+
+#include "fga_kernels.h"
+#include "host_util.h"
+
+namespace fga {
+namespace {
+
+constexpr int kConvThreads = 256;
+constexpr int kSlabPairs = 32;  // channel pairs per warp tile (64 channels)
+
+template <typename T> struct PairOps;
+template <> struct PairOps<__half> {
+    using P = __half2;
+    static __device__ __forceinline__ P fma(P x, P w, P acc) { return __hfma2(x, w, acc); }
+    static __device__ __forceinline__ float2 to_float2(P v) { return __half22float2(v); }
+    static __device__ __forceinline__ P from_float2(float a, float b) {
+        return __floats2half2_rn(a, b);
+    }
+    static __device__ __forceinline__ P zero() { return __float2half2_rn(0.0f); }
+};
+template <> struct PairOps<__nv_bfloat16> {
+    using P = __nv_bfloat162;
+    static __device__ __forceinline__ P fma(P x, P w, P acc) { return __hfma2(x, w, acc); }
+    static __device__ __forceinline__ float2 to_float2(P v) { return __bfloat1622float2(v); }
+    static __device__ __forceinline__ P from_float2(float a, float b) {
+        return __floats2bfloat162_rn(a, b);
+    }
+    static __device__ __forceinline__ P zero() { return __float2bfloat162_rn(0.0f); }
+};
+template <> struct PairOps<float> {
+    using P = float2;
+    static __device__ __forceinline__ P fma(P x, P w, P acc) {
+        return make_float2(fmaf(x.x, w.x, acc.x), fmaf(x.y, w.y, acc.y));
+    }
+    static __device__ __forceinline__ float2 to_float2(P v) { return v; }
+    static __device__ __forceinline__ P from_float2(float a, float b) { return make_float2(a, b); }
+    static __device__ __forceinline__ P zero() { return make_float2(0.0f, 0.0f); }
+};
+
+// SiLU and Swoosh-R (softplus(v - 1) - 0.08 v - 0.313261687), evaluated in fp32 with the
+// same operations as the reference kernels.
+enum Activation : int { kSilu = 0, kSwooshR = 1 };
+
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + __expf(-v)); }
+
+__device__ __forceinline__ float swoosh_r(float v) {
+    const float shifted = v - 1.0f;
+    const float softplus = fmaxf(shifted, 0.0f) + log1pf(__expf(-fabsf(shifted)));
+    return softplus - 0.08f * v - 0.313261687f;
+}
+
+template <typename T, int kAct>
+__device__ __forceinline__ typename PairOps<T>::P activate(typename PairOps<T>::P v) {
+    const float2 f = PairOps<T>::to_float2(v);
+    if constexpr (kAct == kSilu) return PairOps<T>::from_float2(silu(f.x), silu(f.y));
+    else return PairOps<T>::from_float2(swoosh_r(f.x), swoosh_r(f.y));
+}
+
+template <typename T> __device__ __forceinline__ typename PairOps<T>::P load_pair(const T* p) {
+    return *reinterpret_cast<const typename PairOps<T>::P*>(p);
+}
+
+// Frames per warp tile: 16 for the packed 16-bit types, 8 for fp32 (twice the registers
+// per pair).
+template <typename T> __host__ __device__ constexpr int frames_per_tile() { return sizeof(T) == 4 ? 8 : 16; }
+
+// Compile-time tap count kK (the kernel sizes of the encoders: 9, 15, 31). Taps are the
+// outer loop: for tap k every output frame j of the tile takes input frame f0 + j + k - pad,
+// so the inputs form a window of kFrames frames that slides by one frame per tap (one load
+// per tap) and each accumulator still receives its taps in tap order. Weights up to 15 taps
+// stay in registers for the warp's run; longer kernels read each tap's weight once per tile
+// (through L1: every warp of a slab reads the same 128 bytes).
+template <typename T, int kK, int kAct, bool kSkip>
+__global__ void __launch_bounds__(kConvThreads)
+depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
+                      const T* __restrict__ w, const T* __restrict__ bias, T* __restrict__ y,
+                      int batch, int seq, int channels, int tiles, int64_t tasks) {
+    using Ops = PairOps<T>;
+    using P = typename Ops::P;
+    constexpr int kFrames = frames_per_tile<T>();
+    constexpr int kPad = kK / 2;
+    constexpr bool kWeightsInRegs = kK <= 15;
+    constexpr int kRegTaps = kWeightsInRegs ? kK : 1;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int64_t per = (tasks + nwarps - 1) / nwarps;
+    const int64_t t_begin = warp_id * per;
+    const int64_t t_end = t_begin + per < tasks ? t_begin + per : tasks;
+    const int npairs = channels / 2;
+    const int64_t per_slab = static_cast<int64_t>(batch) * tiles;
+
+    P wr[kRegTaps], b0 = Ops::zero();
+    int cur_slab = -1;
+    for (int64_t task = t_begin; task < t_end; ++task) {
+        const int slab = static_cast<int>(task / per_slab);
+        const int64_t rem = task - slab * per_slab;
+        const int n = static_cast<int>(rem / tiles);
+        const int f0 = static_cast<int>(rem - static_cast<int64_t>(n) * tiles) * kFrames;
+        const int p = slab * kSlabPairs + lane;
+        const bool ok = p < npairs;
+        const T* wp = w + 2 * p;
+        if (slab != cur_slab) {
+            if constexpr (kWeightsInRegs) {
+#pragma unroll
+                for (int k = 0; k < kK; ++k)
+                    wr[k] = ok ? load_pair(wp + static_cast<int64_t>(k) * channels) : Ops::zero();
+            }
+            b0 = ok ? load_pair(bias + 2 * p) : Ops::zero();
+            cur_slab = slab;
+        }
+        const int requested = __ldg(lens + n);
+        const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
+        const T* xp = x + static_cast<int64_t>(n) * seq * channels + 2 * p;
+        auto load_frame = [&](int fi) {
+            const bool valid = ok && static_cast<unsigned>(fi) < static_cast<unsigned>(vl);
+            return valid ? load_pair(xp + static_cast<int64_t>(fi) * channels) : Ops::zero();
+        };
+        P acc[kFrames], win[kFrames];
+#pragma unroll
+        for (int j = 0; j < kFrames; ++j) {
+            acc[j] = b0;
+            win[j] = load_frame(f0 - kPad + j);
+        }
+#pragma unroll
+        for (int k = 0; k < kK; ++k) {
+            const P wk = kWeightsInRegs ? wr[k < kRegTaps ? k : 0]
+                                        : (ok ? load_pair(wp + static_cast<int64_t>(k) * channels)
+                                              : Ops::zero());
+            // win[(j + k) % kFrames] holds input frame f0 - kPad + j + k.
+#pragma unroll
+            for (int j = 0; j < kFrames; ++j) {
+                const int fi = f0 - kPad + j + k;
+                if (kSkip && static_cast<unsigned>(fi) >= static_cast<unsigned>(vl)) continue;
+                acc[j] = Ops::fma(win[(j + k) % kFrames], wk, acc[j]);
+            }
+            // Slide: the slot of frame f0 - kPad + k takes frame f0 - kPad + k + kFrames.
+            if (k + 1 < kK) win[k % kFrames] = load_frame(f0 - kPad + k + kFrames);
+        }
+        T* yp = y + (static_cast<int64_t>(n) * seq + f0) * channels + 2 * p;
+        if (ok) {
+#pragma unroll
+            for (int j = 0; j < kFrames; ++j)
+                if (f0 + j < seq)
+                    *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) =
+                        activate<T, kAct>(acc[j]);
+        }
+    }
+}
+
+// Any odd tap count: one output frame pair per thread per step, weights read per tap
+// (through L1), the same per-output arithmetic and order.
+template <typename T, int kAct, bool kSkip>
+__global__ void __launch_bounds__(kConvThreads)
+depthwise_conv_any_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
+                          const T* __restrict__ w, const T* __restrict__ bias, T* __restrict__ y,
+                          int batch, int seq, int channels, int taps) {
+    using Ops = PairOps<T>;
+    using P = typename Ops::P;
+    const int npairs = channels / 2;
+    const int64_t total = static_cast<int64_t>(batch) * seq * npairs;
+    const int pad = taps / 2;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(i % npairs);
+        const int64_t frame_index = i / npairs;
+        const int f = static_cast<int>(frame_index % seq);
+        const int n = static_cast<int>(frame_index / seq);
+        const int requested = __ldg(lens + n);
+        const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
+        P acc = load_pair(bias + 2 * p);
+        for (int k = 0; k < taps; ++k) {
+            const int fi = f + k - pad;
+            const bool valid = static_cast<unsigned>(fi) < static_cast<unsigned>(vl);
+            if (kSkip && !valid) continue;
+            const P xv = valid ? load_pair(x + (static_cast<int64_t>(n) * seq + fi) * channels + 2 * p)
+                               : Ops::zero();
+            acc = Ops::fma(xv, load_pair(w + static_cast<int64_t>(k) * channels + 2 * p), acc);
+        }
+        *reinterpret_cast<P*>(y + frame_index * channels + 2 * p) = activate<T, kAct>(acc);
+    }
+}
+
+// Resident blocks per SM of a kernel, looked up once per (kernel, device).
+template <typename Kernel> int blocks_per_sm(Kernel kernel) {
+    static std::atomic<int> cache[kMaxCachedDevices];
+    const int dev = current_device();
+    if (dev >= 0 && dev < kMaxCachedDevices) {
+        if (const int v = cache[dev].load(std::memory_order_relaxed)) return v;
+    }
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kConvThreads, 0) != cudaSuccess ||
+        v < 1)
+        v = 1;
+    if (dev >= 0 && dev < kMaxCachedDevices) cache[dev].store(v, std::memory_order_relaxed);
+    return v;
+}
+
+template <typename T, int kK, int kAct, bool kSkip>
+cudaError_t launch_fixed(const ConvolutionProblem& p, cudaStream_t stream) {
+    constexpr int kFrames = frames_per_tile<T>();
+    const int tiles = (p.length + kFrames - 1) / kFrames;
+    const int slabs = (p.channels / 2 + kSlabPairs - 1) / kSlabPairs;
+    const int64_t tasks = static_cast<int64_t>(slabs) * p.batch * tiles;
+    auto kernel = depthwise_conv_kernel<T, kK, kAct, kSkip>;
+    const int sms = sm_count();
+    if (sms <= 0) return cudaErrorNotSupported;
+    const int64_t warps_per_block = kConvThreads / 32;
+    int64_t grid = static_cast<int64_t>(sms) * blocks_per_sm(kernel);
+    const int64_t needed = (tasks + warps_per_block - 1) / warps_per_block;
+    if (grid > needed) grid = needed;
+    kernel<<<static_cast<unsigned>(grid), kConvThreads, 0, stream>>>(
+        static_cast<const T*>(p.x), p.valid_lengths, static_cast<const T*>(p.weight),
+        static_cast<const T*>(p.bias), static_cast<T*>(p.output), p.batch, p.length, p.channels,
+        tiles, tasks);
+    return cudaGetLastError();
+}
+
+template <typename T, int kAct, bool kSkip>
+cudaError_t launch_any(const ConvolutionProblem& p, cudaStream_t stream) {
+    const int64_t total = static_cast<int64_t>(p.batch) * p.length * (p.channels / 2);
+    const int sms = sm_count();
+    if (sms <= 0) return cudaErrorNotSupported;
+    auto kernel = depthwise_conv_any_kernel<T, kAct, kSkip>;
+    int64_t grid = static_cast<int64_t>(sms) * blocks_per_sm(kernel);
+    const int64_t needed = (total + kConvThreads - 1) / kConvThreads;
+    if (grid > needed) grid = needed;
+    kernel<<<static_cast<unsigned>(grid), kConvThreads, 0, stream>>>(
+        static_cast<const T*>(p.x), p.valid_lengths, static_cast<const T*>(p.weight),
+        static_cast<const T*>(p.bias), static_cast<T*>(p.output), p.batch, p.length, p.channels,
+        p.taps);
+    return cudaGetLastError();
+}
+
+template <typename T, int kAct, bool kSkip>
+cudaError_t launch_typed(const ConvolutionProblem& p, cudaStream_t stream, const char** variant) {
+    switch (p.taps) {
+        case 9: *variant = "conv-k9"; return launch_fixed<T, 9, kAct, kSkip>(p, stream);
+        case 15: *variant = "conv-k15"; return launch_fixed<T, 15, kAct, kSkip>(p, stream);
+        case 31: *variant = "conv-k31"; return launch_fixed<T, 31, kAct, kSkip>(p, stream);
+        default: *variant = "conv-any"; return launch_any<T, kAct, kSkip>(p, stream);
+    }
+}
+
+template <int kAct, bool kSkip>
+cudaError_t launch_dtype(const ConvolutionProblem& p, cudaStream_t stream, const char** variant) {
+    switch (p.dtype) {
+        case 1: return launch_typed<__half, kAct, kSkip>(p, stream, variant);
+        case 7: return launch_typed<__nv_bfloat16, kAct, kSkip>(p, stream, variant);
+        default: return launch_typed<float, kAct, kSkip>(p, stream, variant);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_convolution(const ConvolutionProblem& p, cudaStream_t stream,
+                               const char** variant) {
+    if (p.kind == ConvolutionProblem::kZipformer) return launch_dtype<kSwooshR, false>(p, stream, variant);
+    // The reference's Parakeet kernels multiply padded taps as zeros only in the packed
+    // eight-channel path (f16/bf16 with C % 8 == 0); the others skip them.
+    const bool zero_taps = p.dtype != 0 && p.channels % 8 == 0;
+    return zero_taps ? launch_dtype<kSilu, false>(p, stream, variant)
+                     : launch_dtype<kSilu, true>(p, stream, variant);
+}
+
+}  // namespace fga

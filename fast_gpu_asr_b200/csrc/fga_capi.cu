@@ -5,6 +5,8 @@
 //   parakeet:  parakeet_relative_attention_plugin.cu:237-290 (haveValidShapes)
 //   zipformer: zipformer_relative_attention_plugin.cu:96-133 (haveValidShapes)
 //   value:     zipformer_attention_value_plugin.cu:79-94 (haveValidShapes)
+//   convolutions: parakeet_convolution_plugin.cu:85-103, zipformer_convolution_plugin.cu:130-150
+//              (haveValidShapes, the same relations in both)
 // and the field checks of their creators (parakeet…cu:1206-1211,
 // zipformer_attention_value…cu:639-650).
 #include <cmath>
@@ -12,6 +14,7 @@
 #include <limits>
 
 #include "../../include/fga_attention.h"
+#include "../../include/fga_convolution.h"
 #include "fga_kernels.h"
 #include "host_util.h"
 
@@ -228,6 +231,39 @@ int32_t check_fused(const fga_tensor_desc* in, int32_t nin, const fga_tensor_des
 
 // The work-counter workspace of the Zipformer weights and fused entry points: present,
 // large enough and aligned for 32-bit atomics.
+// Depthwise-convolution plugins: x [N, T, C], valid_lengths [N] int32, weight [K, C],
+// bias [C], output [N, T, C]; K odd; C a multiple of the reference's vector width (4 for
+// fp32, 2 for f16/bf16); every dim in [1, INT32_MAX] and the byte sizes in int64.
+int32_t check_convolution(const fga_tensor_desc* in, int32_t nin, const fga_tensor_desc* out,
+                          int32_t nout, int32_t kind, fga::ConvolutionProblem* prob) {
+    if (in == nullptr || out == nullptr) return FGA_ERROR_NULL_POINTER;
+    if (nin != 4 || nout != 1) return FGA_ERROR_BAD_DESCRIPTOR;
+    const fga_tensor_desc &x = in[0], &len = in[1], &w = in[2], &b = in[3], &o = out[0];
+    if (x.nb_dims != 3 || len.nb_dims != 1 || w.nb_dims != 2 || b.nb_dims != 1 || o.nb_dims != 3)
+        return FGA_ERROR_BAD_DESCRIPTOR;
+    const int32_t t = x.type;
+    if (!is_float_type(t) || len.type != FGA_INT32 || w.type != t || b.type != t || o.type != t)
+        return FGA_ERROR_BAD_DESCRIPTOR;
+    for (int i = 0; i < 4; ++i)
+        if (!addressable(in[i], true)) return FGA_ERROR_OVERFLOW;
+    if (!addressable(o, true)) return FGA_ERROR_OVERFLOW;
+    const int64_t batch = x.dims[0], length = x.dims[1], channels = x.dims[2], taps = w.dims[0];
+    const int64_t width = t == FGA_FLOAT ? 4 : 2;
+    if (len.dims[0] != batch || taps % 2 != 1 || w.dims[1] != channels || b.dims[0] != channels ||
+        channels % width != 0 || o.dims[0] != batch || o.dims[1] != length ||
+        o.dims[2] != channels)
+        return FGA_ERROR_BAD_SHAPE;
+    if (prob != nullptr) {
+        prob->batch = static_cast<int32_t>(batch);
+        prob->length = static_cast<int32_t>(length);
+        prob->channels = static_cast<int32_t>(channels);
+        prob->taps = static_cast<int32_t>(taps);
+        prob->dtype = t;
+        prob->kind = kind;
+    }
+    return FGA_SUCCESS;
+}
+
 int32_t check_sched_workspace(void* workspace, size_t bytes) {
     if (workspace == nullptr || bytes < FGA_SCHED_WORKSPACE_BYTES ||
         (reinterpret_cast<uintptr_t>(workspace) & 3u) != 0)
@@ -239,6 +275,35 @@ int32_t check_sched_workspace(void* workspace, size_t bytes) {
 // launching (parakeet…cu:948-952), launch, report the launch status.
 int32_t prior_error_status() {
     return cudaPeekAtLastError() == cudaSuccess ? FGA_SUCCESS : FGA_ERROR_PRIOR_CUDA_ERROR;
+}
+
+int32_t convolution_enqueue(const fga_tensor_desc* in, const fga_tensor_desc* out,
+                            const void* const* inputs, void* const* outputs, int32_t kind,
+                            void* stream) {
+    fga::ConvolutionProblem p{};
+    int32_t st = check_convolution(in, 4, out, 1, kind, &p);
+    if (st != FGA_SUCCESS) return st;
+    if (inputs == nullptr || outputs == nullptr || outputs[0] == nullptr)
+        return FGA_ERROR_NULL_POINTER;
+    for (int i = 0; i < 4; ++i)
+        if (inputs[i] == nullptr) return FGA_ERROR_NULL_POINTER;
+    // The kernels move channel pairs: every buffer aligned to two elements.
+    const uintptr_t align = p.dtype == FGA_FLOAT ? 8u : 4u;
+    for (const void* q : {inputs[0], inputs[2], inputs[3], static_cast<const void*>(outputs[0])})
+        if ((reinterpret_cast<uintptr_t>(q) & (align - 1)) != 0) return FGA_ERROR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(inputs[1]) & 3u) != 0) return FGA_ERROR_UNSUPPORTED;
+    if ((st = prior_error_status()) != FGA_SUCCESS) return st;
+    if (!fga::device_is_sm100()) return FGA_ERROR_NO_DEVICE;
+    p.x = inputs[0];
+    p.valid_lengths = static_cast<const int32_t*>(inputs[1]);
+    p.weight = inputs[2];
+    p.bias = inputs[3];
+    p.output = outputs[0];
+    const char* variant = "none";
+    if (fga::launch_convolution(p, static_cast<cudaStream_t>(stream), &variant) != cudaSuccess)
+        return FGA_ERROR_LAUNCH;
+    t_last_variant = variant;
+    return FGA_SUCCESS;
 }
 
 }  // namespace
@@ -466,6 +531,40 @@ int32_t fga_zipformer_attention_fused_enqueue(const fga_tensor_desc* in,
     if (e != cudaSuccess) return FGA_ERROR_LAUNCH;
     t_last_variant = "tcgen05";
     return FGA_SUCCESS;
+}
+
+// ---- depthwise convolutions ---------------------------------------------------------------
+
+int32_t fga_parakeet_conformer_convolution_check(const fga_tensor_desc* in, int32_t nin,
+                                                 const fga_tensor_desc* out, int32_t nout) {
+    return check_convolution(in, nin, out, nout, fga::ConvolutionProblem::kParakeet, nullptr);
+}
+
+size_t fga_parakeet_conformer_convolution_workspace_size(const fga_tensor_desc*, int32_t) {
+    return 0;
+}
+
+int32_t fga_parakeet_conformer_convolution_enqueue(const fga_tensor_desc* in,
+                                                   const fga_tensor_desc* out,
+                                                   const void* const* inputs,
+                                                   void* const* outputs, void*, size_t,
+                                                   void* stream) {
+    return convolution_enqueue(in, out, inputs, outputs, fga::ConvolutionProblem::kParakeet,
+                               stream);
+}
+
+int32_t fga_zipformer_convolution_check(const fga_tensor_desc* in, int32_t nin,
+                                        const fga_tensor_desc* out, int32_t nout) {
+    return check_convolution(in, nin, out, nout, fga::ConvolutionProblem::kZipformer, nullptr);
+}
+
+size_t fga_zipformer_convolution_workspace_size(const fga_tensor_desc*, int32_t) { return 0; }
+
+int32_t fga_zipformer_convolution_enqueue(const fga_tensor_desc* in, const fga_tensor_desc* out,
+                                          const void* const* inputs, void* const* outputs,
+                                          void*, size_t, void* stream) {
+    return convolution_enqueue(in, out, inputs, outputs, fga::ConvolutionProblem::kZipformer,
+                               stream);
 }
 
 }  // extern "C"

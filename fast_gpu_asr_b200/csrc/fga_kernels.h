@@ -56,12 +56,28 @@ struct ZipformerValueProblem {
     int32_t dtype;
 };
 
+// Depthwise temporal convolution of an encoder convolution module (Parakeet Conformer:
+// SiLU; Zipformer: Swoosh-R).
+struct ConvolutionProblem {
+    enum Kind : int32_t { kParakeet = 0, kZipformer = 1 };
+    const void* x;                 // [N, T, C]
+    const int32_t* valid_lengths;  // [N]
+    const void* weight;            // [K, C]
+    const void* bias;              // [C]
+    void* output;                  // [N, T, C]
+    int32_t batch, length, channels, taps;
+    int32_t dtype;
+    int32_t kind;
+};
+
 // Each launcher returns cudaSuccess or the launch error, and records the variant.
 cudaError_t launch_parakeet(const ParakeetProblem& p, cudaStream_t stream, const char** variant);
 cudaError_t launch_zipformer_weights(const ZipformerWeightsProblem& p, cudaStream_t stream,
                                      const char** variant);
 cudaError_t launch_zipformer_value(const ZipformerValueProblem& p, cudaStream_t stream,
                                    const char** variant);
+cudaError_t launch_convolution(const ConvolutionProblem& p, cudaStream_t stream,
+                               const char** variant);
 // Tensor cores only: cudaErrorNotSupported outside the envelope (f16/bf16, qd = 32,
 // T <= 768, vd a multiple of 4 up to 16, H*vd a multiple of 8, aligned buffers).
 cudaError_t launch_zipformer_fused(const ZipformerFusedProblem& p, cudaStream_t stream);

@@ -38,6 +38,11 @@ ZIPFORMER_STACKS = (
     (4, 188, 384, 4, 4),
     (2, 375, 256, 4, 2),
 )
+# Depthwise-convolution kernel size per stack (cnn_module_kernel of the reference's
+# Zipformer fixture, tests/export/test_export_zipformer.py:135-147); Parakeet FastConformer's
+# conv module uses kernel 9 at d_model 1024.
+ZIPFORMER_CONV_KERNELS = (31, 31, 15, 15, 15, 31)
+PARAKEET_CONV_KERNEL = 9
 ZIPFORMER_QUERY_DIM = 32
 ZIPFORMER_VALUE_DIM = 12
 ZIPFORMER_POS_DIM = 48

@@ -1,4 +1,5 @@
-"""CPU oracle for the encoder self-attention hot path (test infrastructure only).
+"""CPU oracle for the encoder self-attention hot path and the convolution-module plugins
+(test infrastructure only).
 
 Imported only by ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline legs of
 ``bench.py``; the ``fast_gpu_asr_b200`` package never imports it.
@@ -11,3 +12,4 @@ from .attention_oracle import (  # noqa: F401
     zipformer_attention_value,
     zipformer_relative_attention,
 )
+from .convolution_oracle import depthwise_convolution  # noqa: F401,E402

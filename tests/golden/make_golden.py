@@ -16,6 +16,16 @@ imports only the two attention modules, which need nothing but torch:
 and, for ``positional_tables.npz``, the two positional encodings
 (``RelPositionalEncoding``, ``CompactRelPositionalEncoding``, zipformer/attention.py:292-374).
 
+The convolution fixtures (``conv_*.npz``) come from the two convolution modules,
+``ConformerConvolution`` (``export/model/parakeet/parakeet.py:495-582``) and
+``ConvolutionModule`` (``export/model/zipformer/zipformer.py:511-573``). Each module runs
+twice on the same input: once with ONNX export simulated (``torch.onnx.is_in_onnx_export``
+patched to True and ``torch.onnx.ops.symbolic`` replaced by a recorder), which captures
+exactly the tensors the module hands to its TensorRT plugin - for Parakeet the depthwise
+weights and bias with the BatchNorm folded in by the module's own export code - and once
+eagerly, with the output projection set to the identity, which gives the plugin-boundary
+output in fp32.
+
 Each fixture stores the plugin-boundary inputs (the projections the modules feed to
 their TensorRT plugins) and the module's eager output at that boundary. Output
 projections are set to (an embedding of) the identity so the module output equals
@@ -45,6 +55,64 @@ def import_reference(reference: Path):
     from fast_gpu_asr.export.model.zipformer import attention as zipformer
 
     return zipformer, parakeet
+
+
+def import_reference_models():
+    """The model modules holding the convolution modules (after import_reference)."""
+    from fast_gpu_asr.export.model.parakeet import parakeet as parakeet_model
+    from fast_gpu_asr.export.model.zipformer import zipformer as zipformer_model
+
+    return zipformer_model, parakeet_model
+
+
+def capture_plugin_inputs(module, x, lengths):
+    """Run ``module`` as under ONNX export and return the tensors it passes to its plugin."""
+    captured = {}
+
+    def symbolic(name, inputs, attrs=None, **kwargs):
+        captured["name"] = name
+        captured["inputs"] = [t.detach().clone() for t in inputs]
+        return torch.zeros(kwargs["shape"], dtype=kwargs["dtype"])
+
+    saved = (torch.onnx.is_in_onnx_export, torch.onnx.ops.symbolic)
+    torch.onnx.is_in_onnx_export = lambda: True
+    torch.onnx.ops.symbolic = symbolic
+    try:
+        with torch.no_grad():
+            module(x, lengths)
+    finally:
+        torch.onnx.is_in_onnx_export, torch.onnx.ops.symbolic = saved
+    return captured
+
+
+def conv_case(model_mod, kind, name, n, t, channels, kernel, seed, lengths) -> None:
+    """Plugin-boundary inputs and eager fp32 output of one convolution module."""
+    torch.manual_seed(seed)
+    if kind == "parakeet":
+        module = model_mod.ConformerConvolution(channels, kernel, True)
+        out_proj = module.pointwise_conv2
+        with torch.no_grad():
+            bn = module.batch_norm
+            bn.weight.uniform_(0.5, 1.5)
+            bn.bias.normal_(0.0, 0.1)
+            bn.running_mean.normal_(0.0, 0.2)
+            bn.running_var.uniform_(0.5, 2.0)
+    else:
+        module = model_mod.ConvolutionModule(channels, kernel)
+        out_proj = module.out_proj
+    module.eval()
+    embed_identity(out_proj)
+    x = torch.randn(n, t, channels)
+    lens = torch.tensor(lengths, dtype=torch.int32)
+    captured = capture_plugin_inputs(module, x, lens)
+    with torch.no_grad():
+        eager = module(x, lens)
+    px, plens, weight, bias = captured["inputs"]
+    np.savez_compressed(
+        HERE / f"{name}.npz", plugin=np.array(captured["name"]), x=f32(px),
+        valid_lengths=plens.numpy().astype(np.int32), weight=f32(weight), bias=f32(bias),
+        output=f32(eager))
+    print(name, captured["name"], tuple(px.shape), tuple(weight.shape))
 
 
 def suffix_mask(lengths, t):
@@ -194,6 +262,15 @@ def main() -> None:
     parakeet_case(par_mod, "parakeet_h1_d128_t160_fp16", "float16", 1, 160, 1, 128, seed=24,
                   lengths=(137,))
     positional_tables(zip_mod, par_mod)
+    zip_model, par_model = import_reference_models()
+    conv_case(par_model, "parakeet", "conv_parakeet_k9_c64", 3, 41, 64, 9, seed=31,
+              lengths=(41, 17, 0))
+    conv_case(par_model, "parakeet", "conv_parakeet_k9_c38", 2, 23, 38, 9, seed=32,
+              lengths=(23, 5))
+    conv_case(zip_model, "zipformer", "conv_zipformer_k31_c48", 3, 70, 48, 31, seed=33,
+              lengths=(70, 44, 1))
+    conv_case(zip_model, "zipformer", "conv_zipformer_k15_c40", 2, 19, 40, 15, seed=34,
+              lengths=(12, 19))
 
 
 if __name__ == "__main__":

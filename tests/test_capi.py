@@ -19,20 +19,22 @@ import pytest
 from fast_gpu_asr_b200 import _lib
 from fast_gpu_asr_b200 import attention as ops
 
-HEADER = Path(__file__).resolve().parents[1] / "include" / "fga_attention.h"
+HEADERS = sorted((Path(__file__).resolve().parents[1] / "include").glob("*.h"))
 F32, F16, BF16, I32, BOOL = _lib.FGA_FLOAT, _lib.FGA_HALF, _lib.FGA_BF16, _lib.FGA_INT32, _lib.FGA_BOOL
 D = _lib.TensorDesc.make
 
 
 def declared_symbols() -> set[str]:
-    text = HEADER.read_text()
+    text = "\n".join(h.read_text() for h in HEADERS)
     return set(re.findall(r"FGA_API\s+[\w\s\*]+?\b(fga_\w+)\s*\(", text))
 
 
 def test_header_declares_the_entry_points():
     names = declared_symbols()
+    assert [h.name for h in HEADERS] == ["fga_attention.h", "fga_convolution.h"]
     for op in ("parakeet_relative_attention", "zipformer_relative_attention",
-               "zipformer_attention_value"):
+               "zipformer_attention_value", "parakeet_conformer_convolution",
+               "zipformer_convolution"):
         for suffix in ("check", "workspace_size", "enqueue"):
             assert f"fga_{op}_{suffix}" in names
     assert {"fga_abi_version", "fga_status_string", "fga_last_kernel_variant"} <= names
@@ -63,7 +65,7 @@ def test_workspace_sizes(library):
             == _lib.SCHED_WORKSPACE_BYTES)
     assert (library.fga_zipformer_attention_fused_workspace_size(descs, 2)
             == _lib.SCHED_WORKSPACE_BYTES)
-    header = HEADER.read_text()
+    header = HEADERS[0].read_text()
     assert f"#define FGA_SCHED_WORKSPACE_BYTES {_lib.SCHED_WORKSPACE_BYTES}" in header
 
 
