@@ -97,12 +97,16 @@ template <typename T> __device__ __forceinline__ typename PairOps<T>::P load_pai
 // per pair).
 template <typename T> __host__ __device__ constexpr int frames_per_tile() { return sizeof(T) == 4 ? 8 : 16; }
 
-// Compile-time tap count kK (the kernel sizes of the encoders: 9, 15, 31). Taps are the
-// outer loop: for tap k every output frame j of the tile takes input frame f0 + j + k - pad,
-// so the inputs form a window of kFrames frames that slides by one frame per tap (one load
-// per tap) and each accumulator still receives its taps in tap order. Weights up to 15 taps
-// stay in registers for the warp's run; longer kernels read each tap's weight once per tile
-// (through L1: every warp of a slab reads the same 128 bytes).
+// Compile-time tap count kK (the kernel sizes of the encoders: 9, 15, 31).
+//
+// Block tile: 64 channels x kBlockFrames output frames of one utterance. The block stages
+// the tile's input frames (kBlockFrames + kK - 1 rows of 64 channels, zeros where a frame is
+// padded or outside [0, T)) and the slab's weights in shared memory, then warp w computes
+// kFrames of the output frames with lane l on channel pair l. Taps are the outer loop: for
+// tap k output frame j takes staged row j + k, so a warp's rows form a window of kFrames
+// that slides by one row per tap (one shared-memory load per tap) and every accumulator
+// receives its taps in tap order. Weights up to 15 taps stay in registers for the block's
+// run of tiles of one slab; longer kernels read each tap's weight from shared memory.
 template <typename T, int kK, int kAct, bool kSkip>
 __global__ void __launch_bounds__(kConvThreads)
 depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
@@ -111,17 +115,26 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
     using Ops = PairOps<T>;
     using P = typename Ops::P;
     constexpr int kFrames = frames_per_tile<T>();
+    constexpr int kBlockFrames = (kConvThreads / 32) * kFrames;
+    constexpr int kRows = kBlockFrames + kK - 1;
     constexpr int kPad = kK / 2;
+    constexpr int kRowBytes = kSlabPairs * static_cast<int>(sizeof(P));
+    constexpr int kChunks = kRowBytes / 16;                      // 16-byte pieces of a row
+    constexpr int kChunkElems = 16 / static_cast<int>(sizeof(T));
     constexpr bool kWeightsInRegs = kK <= 15;
     constexpr int kRegTaps = kWeightsInRegs ? kK : 1;
-    const int lane = threadIdx.x & 31;
-    const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    const int64_t per = (tasks + nwarps - 1) / nwarps;
-    const int64_t t_begin = warp_id * per;
-    const int64_t t_end = t_begin + per < tasks ? t_begin + per : tasks;
+    __shared__ __align__(16) unsigned char s_x[kRows * kRowBytes];
+    __shared__ __align__(16) unsigned char s_w[kK * kRowBytes];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int npairs = channels / 2;
     const int64_t per_slab = static_cast<int64_t>(batch) * tiles;
+    const int64_t per = (tasks + gridDim.x - 1) / gridDim.x;
+    const int64_t t_begin = static_cast<int64_t>(blockIdx.x) * per;
+    const int64_t t_end = t_begin + per < tasks ? t_begin + per : tasks;
+    // 16-byte staging needs every row piece aligned: 8 (16-bit) or 4 (fp32) channels.
+    const bool vec16 = (channels % kChunkElems) == 0 &&
+                       (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 
     P wr[kRegTaps], b0 = Ops::zero();
     int cur_slab = -1;
@@ -129,52 +142,82 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         const int slab = static_cast<int>(task / per_slab);
         const int64_t rem = task - slab * per_slab;
         const int n = static_cast<int>(rem / tiles);
-        const int f0 = static_cast<int>(rem - static_cast<int64_t>(n) * tiles) * kFrames;
+        const int f0 = static_cast<int>(rem - static_cast<int64_t>(n) * tiles) * kBlockFrames;
         const int p = slab * kSlabPairs + lane;
         const bool ok = p < npairs;
-        const T* wp = w + 2 * p;
-        if (slab != cur_slab) {
-            if constexpr (kWeightsInRegs) {
-#pragma unroll
-                for (int k = 0; k < kK; ++k)
-                    wr[k] = ok ? load_pair(wp + static_cast<int64_t>(k) * channels) : Ops::zero();
+        const bool new_slab = slab != cur_slab;
+        __syncthreads();  // the previous tile's rows (and weights) are no longer read
+        if (new_slab) {
+            for (int i = tid; i < kK * kSlabPairs; i += kConvThreads) {
+                const int k = i / kSlabPairs, q = slab * kSlabPairs + i % kSlabPairs;
+                *reinterpret_cast<P*>(s_w + i * sizeof(P)) =
+                    q < npairs ? load_pair(w + static_cast<int64_t>(k) * channels + 2 * q)
+                               : Ops::zero();
             }
             b0 = ok ? load_pair(bias + 2 * p) : Ops::zero();
-            cur_slab = slab;
         }
         const int requested = __ldg(lens + n);
         const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
-        const T* xp = x + static_cast<int64_t>(n) * seq * channels + 2 * p;
-        auto load_frame = [&](int fi) {
-            const bool valid = ok && static_cast<unsigned>(fi) < static_cast<unsigned>(vl);
-            return valid ? load_pair(xp + static_cast<int64_t>(fi) * channels) : Ops::zero();
-        };
+        const T* xb = x + static_cast<int64_t>(n) * seq * channels;
+        const int c_slab = slab * 2 * kSlabPairs;  // first channel of the slab
+        if (vec16) {
+            for (int i = tid; i < kRows * kChunks; i += kConvThreads) {
+                const int r = i / kChunks, c = c_slab + (i % kChunks) * kChunkElems;
+                const int fi = f0 - kPad + r;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (static_cast<unsigned>(fi) < static_cast<unsigned>(vl) && c < channels)
+                    v = __ldg(reinterpret_cast<const uint4*>(
+                        xb + static_cast<int64_t>(fi) * channels + c));
+                *reinterpret_cast<uint4*>(s_x + i * 16) = v;
+            }
+        } else {
+            for (int i = tid; i < kRows * kSlabPairs; i += kConvThreads) {
+                const int r = i / kSlabPairs, q = slab * kSlabPairs + i % kSlabPairs;
+                const int fi = f0 - kPad + r;
+                P v = Ops::zero();
+                if (static_cast<unsigned>(fi) < static_cast<unsigned>(vl) && q < npairs)
+                    v = load_pair(xb + static_cast<int64_t>(fi) * channels + 2 * q);
+                *reinterpret_cast<P*>(s_x + i * sizeof(P)) = v;
+            }
+        }
+        __syncthreads();
+        if constexpr (kWeightsInRegs) {
+            if (new_slab) {
+#pragma unroll
+                for (int k = 0; k < kK; ++k)
+                    wr[k] = *reinterpret_cast<const P*>(s_w + k * kRowBytes + lane * sizeof(P));
+            }
+        }
+        cur_slab = slab;
+        const int fw = f0 + warp * kFrames;  // this warp's first output frame
+        const unsigned char* xs = s_x + warp * kFrames * kRowBytes + lane * sizeof(P);
         P acc[kFrames], win[kFrames];
 #pragma unroll
         for (int j = 0; j < kFrames; ++j) {
             acc[j] = b0;
-            win[j] = load_frame(f0 - kPad + j);
+            win[j] = *reinterpret_cast<const P*>(xs + j * kRowBytes);
         }
 #pragma unroll
         for (int k = 0; k < kK; ++k) {
-            const P wk = kWeightsInRegs ? wr[k < kRegTaps ? k : 0]
-                                        : (ok ? load_pair(wp + static_cast<int64_t>(k) * channels)
-                                              : Ops::zero());
-            // win[(j + k) % kFrames] holds input frame f0 - kPad + j + k.
+            P wk;
+            if constexpr (kWeightsInRegs) wk = wr[k < kRegTaps ? k : 0];
+            else wk = *reinterpret_cast<const P*>(s_w + k * kRowBytes + lane * sizeof(P));
+            // win[(j + k) % kFrames] holds staged row j + k (input frame fw - kPad + j + k).
 #pragma unroll
             for (int j = 0; j < kFrames; ++j) {
-                const int fi = f0 - kPad + j + k;
+                const int fi = fw - kPad + j + k;
                 if (kSkip && static_cast<unsigned>(fi) >= static_cast<unsigned>(vl)) continue;
                 acc[j] = Ops::fma(win[(j + k) % kFrames], wk, acc[j]);
             }
-            // Slide: the slot of frame f0 - kPad + k takes frame f0 - kPad + k + kFrames.
-            if (k + 1 < kK) win[k % kFrames] = load_frame(f0 - kPad + k + kFrames);
+            // Slide: the slot of row k takes row k + kFrames.
+            if (k + 1 < kK)
+                win[k % kFrames] = *reinterpret_cast<const P*>(xs + (k + kFrames) * kRowBytes);
         }
-        T* yp = y + (static_cast<int64_t>(n) * seq + f0) * channels + 2 * p;
         if (ok) {
+            T* yp = y + (static_cast<int64_t>(n) * seq + fw) * channels + 2 * p;
 #pragma unroll
             for (int j = 0; j < kFrames; ++j)
-                if (f0 + j < seq)
+                if (fw + j < seq)
                     *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) =
                         activate<T, kAct>(acc[j]);
         }
@@ -231,17 +274,15 @@ template <typename Kernel> int blocks_per_sm(Kernel kernel) {
 
 template <typename T, int kK, int kAct, bool kSkip>
 cudaError_t launch_fixed(const ConvolutionProblem& p, cudaStream_t stream) {
-    constexpr int kFrames = frames_per_tile<T>();
-    const int tiles = (p.length + kFrames - 1) / kFrames;
+    constexpr int kBlockFrames = (kConvThreads / 32) * frames_per_tile<T>();
+    const int tiles = (p.length + kBlockFrames - 1) / kBlockFrames;
     const int slabs = (p.channels / 2 + kSlabPairs - 1) / kSlabPairs;
     const int64_t tasks = static_cast<int64_t>(slabs) * p.batch * tiles;
     auto kernel = depthwise_conv_kernel<T, kK, kAct, kSkip>;
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
-    const int64_t warps_per_block = kConvThreads / 32;
     int64_t grid = static_cast<int64_t>(sms) * blocks_per_sm(kernel);
-    const int64_t needed = (tasks + warps_per_block - 1) / warps_per_block;
-    if (grid > needed) grid = needed;
+    if (grid > tasks) grid = tasks;
     kernel<<<static_cast<unsigned>(grid), kConvThreads, 0, stream>>>(
         static_cast<const T*>(p.x), p.valid_lengths, static_cast<const T*>(p.weight),
         static_cast<const T*>(p.bias), static_cast<T*>(p.output), p.batch, p.length, p.channels,
