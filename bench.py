@@ -1,7 +1,8 @@
 """Encoder-attention benchmark: audio-seconds per second through the attention plugins.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload parakeet|parakeet_long|zipformer|zipformer_fused|ragged]
+                    [--workload parakeet|parakeet_long|zipformer|zipformer_fused|ragged|
+                                parakeet_conv|zipformer_conv]
     python bench.py --impl reference ...   # the reference math on the host cores
 
 A *step* is one encoder forward's worth of attention calls over one batch:
@@ -14,6 +15,14 @@ A *step* is one encoder forward's worth of attention calls over one batch:
   (2/2/4/5/4/2 layers at T = 750/375/188/94/188/375), each layer one
   ``zipformer_relative_attention`` call plus three ``zipformer_attention_value`` calls,
   bf16, 256 utterances.
+* ``parakeet_conv`` / ``zipformer_conv``: the encoders' convolution modules of one pass
+  (Parakeet: 24 ``parakeet_conformer_convolution`` calls at 256 x 375 x 1024, kernel 9,
+  f16; Zipformer: two ``zipformer_convolution`` calls per layer of the config-3 stacks,
+  kernels 31/31/15/15/15/31, bf16).
+
+The default line also carries the other workloads as sub-objects, each with its own
+timed region: ``zipformer``, ``parakeet_long``, ``zipformer_fused``, ``parakeet_conv`` and
+``zipformer_conv``.
 
 ``value`` = audio seconds of all ranks' batches x K / max-over-ranks device time of the
 K steps (CUDA events, inputs resident in HBM). ``e2e`` = the same metric through the
@@ -49,7 +58,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=("parakeet", "parakeet_long", "zipformer",
-                                          "zipformer_fused", "ragged"),
+                                          "zipformer_fused", "ragged", "parakeet_conv",
+                                          "zipformer_conv"),
                    default="parakeet")
     p.add_argument("--batch", type=int, default=None,
                    help="utterances per GPU (default 256; 16 for parakeet_long)")
@@ -413,8 +423,47 @@ def cpu_zipformer(seconds: float):
     return value, torch.get_num_threads(), sample
 
 
+def cpu_convolution(kind: str, seconds: float, per_call: int | None = None):
+    """Time the convolution oracle (the reference plugin arithmetic restated in numpy,
+    storage-precision rounding per tap) on a slice of the conv workload's utterances."""
+    from fast_gpu_asr_b200 import workloads as wl
+    from oracle.convolution_oracle import depthwise_convolution
+
+    if per_call is None:
+        per_call = 2 if kind == "parakeet" else 4
+    rng = np.random.default_rng(5)
+    if kind == "parakeet":
+        lengths = wl.parakeet_lengths(per_call, 375, 60, seed=7)
+        calls = [(rng.normal(0, 1, (per_call, 375, 1024)).astype(np.float32), lengths,
+                  wl.PARAKEET_CONV_KERNEL, 1024, "float16", wl.PARAKEET_LAYERS)]
+        audio = float(lengths.sum()) * wl.PARAKEET_FRAME_SECONDS
+    else:
+        in_lengths = wl.zipformer_input_lengths(per_call, seed=1)
+        calls = [(rng.normal(0, 1, (per_call, t, embed)).astype(np.float32),
+                  wl.zipformer_stack_lengths(in_lengths, ds), wl.ZIPFORMER_CONV_KERNELS[i],
+                  embed, "bfloat16", 2 * nl)
+                 for i, (ds, t, embed, _, nl) in enumerate(wl.ZIPFORMER_STACKS)]
+        audio = float(in_lengths.sum()) * wl.ZIPFORMER_INPUT_FRAME_SECONDS
+    weights = [(rng.normal(0, 0.2, (k, c)).astype(np.float32),
+                rng.normal(0, 0.1, c).astype(np.float32)) for _, _, k, c, _, _ in calls]
+    t0, passes = time.perf_counter(), 0.0
+    while True:
+        # One call per stack (or one Parakeet layer), scaled to the pass's call count.
+        for (x, lens, _, _, dt, reps), (w, b) in zip(calls, weights):
+            depthwise_convolution(x, lens, w, b, kind, dt)
+        passes += 1.0 / sum(c[5] for c in calls) * len(calls)
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    sample = (f"{per_call}-utterance slice, one conv-module call per "
+              + ("layer" if kind == "parakeet" else "stack") + " per pass, scaled to a full pass")
+    return audio * passes / elapsed, 1, sample
+
+
 def cpu_leg(args):
     """The CPU timing function of the workload (seconds -> value, cores, sample)."""
+    if args.workload in ("parakeet_conv", "zipformer_conv"):
+        return lambda seconds: cpu_convolution(args.workload[:-5], seconds)
     if args.workload == "parakeet_long":
         return lambda seconds: cpu_parakeet(seconds, 3000, 1500, 1)
     return cpu_parakeet if args.workload == "parakeet" else cpu_zipformer
@@ -446,6 +495,9 @@ def reference_arm(args, world, rank):
 
 
 def workload_config(args) -> dict:
+    if args.workload in ("parakeet_conv", "zipformer_conv"):
+        return {"workload": args.workload, "batch": args.batch,
+                "dtype": "f16" if args.workload == "parakeet_conv" else "bf16"}
     if args.workload == "parakeet_long":
         return {"workload": "parakeet_relative_attention (config 4, long-form)",
                 "batch": args.batch, "frames": 3000, "heads": 8, "head_dim": 128, "layers": 24,
@@ -484,9 +536,12 @@ def ragged_arm(args, world, rank, local):
     round-robin); per batch the Parakeet stack (24 layers, f16) and the Zipformer stacks
     (bf16); per-batch outputs of both models gathered to rank 0 at the end.
 
-    ``value`` = audio seconds of all utterances / max over ranks of the summed kernel time
-    (CUDA events around each batch's attention calls; inputs are generated on the device
-    between batches, outside the events). The gather is timed separately.
+    ``value`` = audio seconds of all utterances / max over ranks of the summed batch time
+    (CUDA events around each batch's attention calls, host gaps between the launches
+    included; inputs are generated on the device between batches, outside the events).
+    ``rank_launch_ms`` sums the events around each launch instead, which leaves the host
+    gaps out. One small call of each operator before the first batch loads the kernels.
+    The gather is timed separately.
     """
     import torch
 
@@ -505,7 +560,19 @@ def ragged_arm(args, world, rank, local):
     else:
         assignment = [shard_round_robin(len(plan), world, r) for r in range(world)]
     mine = assignment[rank]
-    kernel_ms, outputs, z_outputs, launches = 0.0, {}, {}, 0
+    warm_p = wl.make_parakeet_layer(2, 64, 8, 128, torch.float16, "cuda", seed=1,
+                                    lengths=np.array([64, 33], np.int32))
+    warm_z = wl.make_zipformer_layer(2, 64, 192, 4, torch.bfloat16, "cuda", 1,
+                                     np.array([64, 33], np.int64))
+    with torch.cuda.stream(stream):
+        parakeet_relative_attention(warm_p.qkv, warm_p.position, warm_p.content_bias,
+                                    warm_p.position_bias, warm_p.valid_lengths, warm_p.scale,
+                                    stream=stream)
+        run_zipformer_step([(4, torch.empty((2, 4, 64, 64), dtype=torch.bfloat16, device="cuda"),
+                             [warm_z], (torch.empty_like(warm_z.value_a),
+                                        torch.empty_like(warm_z.nonlin_value)))], stream)
+    stream.synchronize()
+    kernel_ms, launch_ms, outputs, z_outputs, launches = 0.0, 0.0, {}, {}, 0
     shapes, z_shapes = {}, {}
     for b in plan:
         lens = np.maximum(1, np.floor(b.lengths / wl.PARAKEET_FRAME_SECONDS)).astype(np.int32)
@@ -533,19 +600,25 @@ def ragged_arm(args, world, rank, local):
             outs = (torch.empty_like(layers[0].value_a), torch.empty_like(layers[0].nonlin_value))
             stacks.append((heads, weights, [layers[i % 2] for i in range(nlayers)], outs))
         out = torch.empty((len(p_lens), t, 1024), dtype=torch.float16, device="cuda")
+        n_launch = wl.PARAKEET_LAYERS + 4 * sum(len(s[2]) for s in stacks)
+        events = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+                  for _ in range(n_launch)]
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             start.record(stream)
             for i in range(wl.PARAKEET_LAYERS):
                 L = players[i % 2]
+                events[i][0].record(stream)
                 parakeet_relative_attention(L.qkv, L.position, L.content_bias, L.position_bias,
                                             L.valid_lengths, L.scale, out=out, stream=stream)
-            run_zipformer_step(stacks, stream)
+                events[i][1].record(stream)
+            run_zipformer_step(stacks, stream, events[wl.PARAKEET_LAYERS:])
             end.record(stream)
         end.synchronize()
         kernel_ms += start.elapsed_time(end)
-        launches += wl.PARAKEET_LAYERS + 4 * sum(len(s[2]) for s in stacks)
+        launch_ms += sum(e[0].elapsed_time(e[1]) for e in events)
+        launches += n_launch
         outputs[idx] = out
         # The attention outputs of each stack's last layer (self-attention, nonlinear).
         z_outputs[idx] = [t for s in stacks for t in s[3]]
@@ -553,6 +626,7 @@ def ragged_arm(args, world, rank, local):
     barrier(world)
     max_ms = allreduce_max(kernel_ms, world)
     rank_ms = allgather_floats(kernel_ms, world)
+    rank_launch_ms = allgather_floats(launch_ms, world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     gathered = gather_to_rank0(outputs, shapes, world, rank, "cuda", torch.float16, assignment)
@@ -572,6 +646,7 @@ def ragged_arm(args, world, rank, local):
                 "dtype": "f16+bf16", "data": "synthetic", "config": workload_config(args),
                 "batches": len(plan), "batches_per_rank": len(mine), "deal": args.deal,
                 "rank_busy_ms": rank_ms, "rank_busy_spread": max(rank_ms) / max(min(rank_ms), 1e-9),
+                "rank_launch_ms": rank_launch_ms,
                 "gather_wall_s": gather_s, "gathered_bytes": gathered_bytes,
                 "gpu_launches": launches,
                 "variant": _lib.last_kernel_variant()}
@@ -736,8 +811,118 @@ def measure_workload(args, world, rank, local, peaks, *, with_e2e=True, with_cpu
             "clocks": clocks, "audio_seconds_per_step_per_gpu": audio}
 
 
+# ---- convolution modules ---------------------------------------------------------------------
+def build_convolution(kind: str, batch: int, rank: int):
+    """Calls of one encoder step's convolution modules, with their inputs resident:
+    Parakeet config 2 (24 layers, one Conformer conv module each, 256 x 375 x 1024,
+    kernel 9, f16) or Zipformer config 3 (two conv modules per layer, each stack's T,
+    embed dim and kernel, bf16). Layers alternate between two input/output buffer sets, so
+    consecutive calls do not find their inputs in L2 (stack inputs of 5-75 MB; a call's
+    read plus write exceeds the 126 MB L2 for the larger stacks only).
+    Returns (calls, audio seconds per step, algorithmic bytes per step)."""
+    import torch
+
+    from fast_gpu_asr_b200 import workloads as wl
+    from fast_gpu_asr_b200.convolution import parakeet_conformer_convolution, zipformer_convolution
+
+    gen = torch.Generator(device="cuda").manual_seed(4242 + rank)
+
+    def tensors(n, t, c, k, dt, lengths):
+        xs = [torch.randn((n, t, c), generator=gen, device="cuda").to(dt) for _ in range(2)]
+        ys = [torch.empty_like(xs[0]) for _ in range(2)]
+        w = (0.2 * torch.randn((k, c), generator=gen, device="cuda")).to(dt)
+        b = (0.1 * torch.randn((c,), generator=gen, device="cuda")).to(dt)
+        lens = torch.from_numpy(np.asarray(lengths, np.int32)).cuda()
+        return xs, ys, w, b, lens
+
+    calls = []
+    if kind == "parakeet":
+        lengths = wl.parakeet_lengths(batch, 375, 60, seed=7 + rank)
+        xs, ys, w, b, lens = tensors(batch, 375, 1024, wl.PARAKEET_CONV_KERNEL, torch.float16,
+                                     lengths)
+        for i in range(wl.PARAKEET_LAYERS):
+            calls.append((parakeet_conformer_convolution, xs[i % 2], lens, w, b, ys[i % 2]))
+        audio = float(lengths.sum()) * wl.PARAKEET_FRAME_SECONDS
+    else:
+        in_lengths = wl.zipformer_input_lengths(batch, seed=1 + rank)
+        for s_i, (ds, t, embed, _, nlayers) in enumerate(wl.ZIPFORMER_STACKS):
+            lengths = wl.zipformer_stack_lengths(in_lengths, ds)
+            xs, ys, w, b, lens = tensors(batch, t, embed, wl.ZIPFORMER_CONV_KERNELS[s_i],
+                                         torch.bfloat16, lengths)
+            for i in range(2 * nlayers):
+                calls.append((zipformer_convolution, xs[i % 2], lens, w, b, ys[i % 2]))
+        audio = float(in_lengths.sum()) * wl.ZIPFORMER_INPUT_FRAME_SECONDS
+    nbytes = float(sum(2 * c[1].numel() * c[1].element_size() for c in calls))
+    return calls, audio, nbytes
+
+
+def measure_convolution(args, world, rank, local, peaks, kind: str) -> dict:
+    """One step = every conv-module call of an encoder pass; CUDA events around every
+    launch on the launching stream, W warm-up and K timed steps, max over ranks."""
+    import torch
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        value, cores, sample = cpu_convolution(kind, min(3.0, args.cpu_seconds))
+        cpu = {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    calls, audio, nbytes = build_convolution(kind, 256, rank)
+    stream = torch.cuda.Stream()
+
+    def step(events=None):
+        for i, (op, x, lens, w, b, y) in enumerate(calls):
+            if events is not None:
+                events[i][0].record(stream)
+            op(x, lens, w, b, out=y, stream=stream)
+            if events is not None:
+                events[i][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+               for _ in calls] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(device_bus_id(local)) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for k in range(args.steps):
+            step(events[k])
+        end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    barrier(world)
+    max_ms = allreduce_max(start.elapsed_time(end), world)
+    busy_ms = sum(e[0].elapsed_time(e[1]) for ev in events for e in ev)
+    avg_launch_ms = busy_ms / (args.steps * len(calls))
+    achieved = nbytes * args.steps / (busy_ms / 1000.0) / 1e9
+    name = "parakeet_conformer_convolution" if kind == "parakeet" else "zipformer_convolution"
+    return {
+        "value": audio * args.steps * world / (max_ms / 1000.0), "unit": UNIT,
+        "ms_per_step": max_ms / args.steps,
+        "dtype": "f16" if kind == "parakeet" else "bf16",
+        "config": {"workload": f"{kind} conv modules of one encoder pass "
+                               + ("(24 layers, 256 x 375 x 1024, kernel 9)" if kind == "parakeet"
+                                  else "(2 per layer, config-3 stacks, kernels 31,31,15,15,15,31)"),
+                   "batch": 256, "l2": "two buffer sets alternate between layers"},
+        "roofline": {"bound": "hbm", "kernel": name, "achieved": achieved,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"],
+                     "traffic": load_traffic(name, nbytes / len(calls)),
+                     "peak_source": f"{peaks['source']} HBM copy",
+                     "bytes_per_launch": nbytes / len(calls), "avg_launch_ms": avg_launch_ms},
+        "cpu_baseline": cpu, "gpu_launches": len(calls) * args.steps, "clocks": clocks,
+    }
+
+
 # Secondary workloads carried in the default line (same K and W, each its own timed region).
 SECONDARY = ("zipformer", "parakeet_long", "zipformer_fused")
+CONV_SECONDARY = ("parakeet", "zipformer")
 
 
 def ours_arm(args, world, rank, local):
@@ -747,6 +932,15 @@ def ours_arm(args, world, rank, local):
 
     _lib.library()
     peaks = load_peaks()
+    if args.workload in ("parakeet_conv", "zipformer_conv"):
+        # The convolution modules alone (the same measurement the default line carries).
+        sub = measure_convolution(args, world, rank, local, peaks, args.workload[:-5])
+        line = {"metric": "encoder-convolution audio-sec/sec (RTFx)", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "data": "synthetic", **sub}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     line = measure_workload(args, world, rank, local, peaks,
                             with_gpu_reference=args.workload in ("parakeet", "zipformer"))
     if args.workload == "parakeet" and not args.no_secondary:
@@ -759,6 +953,9 @@ def ours_arm(args, world, rank, local):
             line[name] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "dtype", "config",
                                               "roofline", "e2e", "cpu_baseline",
                                               "gpu_reference", "gpu_launches", "clocks")}
+        for kind in CONV_SECONDARY:
+            torch.cuda.empty_cache()
+            line[f"{kind}_conv"] = measure_convolution(args, world, rank, local, peaks, kind)
     if rank == 0:
         print(json.dumps(line), flush=True)
 
