@@ -109,6 +109,8 @@ TRT_SHIMS = (
     "parakeet_relative_attention_plugin",
     "zipformer_relative_attention_plugin",
     "zipformer_attention_value_plugin",
+    "zipformer_convolution_plugin",
+    "parakeet_convolution_plugin",
 )
 
 

@@ -23,11 +23,15 @@ from . import _lib
 
 PLUGIN_DIR = Path(__file__).resolve().parent
 
-# (shared object, exported initializer), as in the reference's constants.py:45-67.
+# (shared object, exported initializer), as in the reference's constants.py:45-67, for
+# the plugins this library implements (the feature, resampling and output-assembly
+# plugins are not part of it).
 PLUGIN_INITIALIZERS = (
     ("zipformer_attention_value_plugin.so", "initFastGpuAsrZipformerAttentionValuePlugin"),
     ("zipformer_relative_attention_plugin.so", "initFastGpuAsrZipformerRelativeAttentionPlugin"),
+    ("zipformer_convolution_plugin.so", "initFastGpuAsrZipformerConvolutionPlugin"),
     ("parakeet_relative_attention_plugin.so", "initFastGpuAsrParakeetRelativeAttentionPlugin"),
+    ("parakeet_convolution_plugin.so", "initFastGpuAsrParakeetConvolutionPlugin"),
 )
 
 

@@ -1,7 +1,8 @@
 """TensorRT plugin shims and their loader, on CPU without TensorRT.
 
 The reference compiles native plugin code against a generated stub TensorRT header in its
-CPU tests (``tests/plugins/test_cublas_tactics.py:33-94``). Here the three shims
+CPU tests (``tests/plugins/test_cublas_tactics.py:33-94``). Here the five shims (three
+attention plugins, two convolution plugins)
 (``fast_gpu_asr_b200/csrc/trt/``) are compiled against ``tests/trt_stub/NvInfer.h``:
 
 * a contract harness (``tests/trt_stub/harness.cpp``) drives them through the IPluginV3
@@ -82,7 +83,7 @@ def run_loader(plugin_dir, registry, env=None):
 def test_loader_registers_every_plugin_once(stub_build):
     out = run_loader(stub_build, stub_build / "libstub_registry.so")
     assert out.returncode == 0, out.stdout + out.stderr
-    assert "REGISTERED 3 3" in out.stdout
+    assert "REGISTERED 5 5" in out.stdout
 
 
 def test_loader_reports_registration_failure(stub_build):
@@ -95,7 +96,8 @@ def test_loader_reports_missing_library_and_initializer(stub_build, tmp_path):
     out = run_loader(tmp_path, stub_build / "libstub_registry.so")
     assert out.returncode == 3 and "Failed to load TensorRT plugin library" in out.stdout
     for name in ("zipformer_attention_value_plugin", "zipformer_relative_attention_plugin",
-                 "parakeet_relative_attention_plugin"):
+                 "zipformer_convolution_plugin", "parakeet_relative_attention_plugin",
+                 "parakeet_convolution_plugin"):
         shutil.copy(stub_build / "libstub_registry.so", tmp_path / f"{name}.so")
     out = run_loader(tmp_path, stub_build / "libstub_registry.so")
     assert out.returncode == 3 and "does not export" in out.stdout
@@ -107,7 +109,11 @@ def test_shims_export_only_their_initializer(stub_build):
                        ("zipformer_relative_attention_plugin",
                         "initFastGpuAsrZipformerRelativeAttentionPlugin"),
                        ("zipformer_attention_value_plugin",
-                        "initFastGpuAsrZipformerAttentionValuePlugin")):
+                        "initFastGpuAsrZipformerAttentionValuePlugin"),
+                       ("zipformer_convolution_plugin",
+                        "initFastGpuAsrZipformerConvolutionPlugin"),
+                       ("parakeet_convolution_plugin",
+                        "initFastGpuAsrParakeetConvolutionPlugin")):
         out = subprocess.run(["nm", "-D", "--defined-only", str(stub_build / f"{name}.so")],
                              capture_output=True, text=True, check=True)
         exported = {line.split()[-1] for line in out.stdout.splitlines() if " T " in line}

@@ -3,7 +3,7 @@
 // registries are in-memory fakes, and the C ABI is a fake that records what each shim
 // forwards. TEST INFRASTRUCTURE ONLY.
 //
-// Checked for each of the three plugins: registration in both registries and idempotent
+// Checked for each of the five plugins: registration in both registries and idempotent
 // re-initialisation; the creator's field validation; identity (name, version "1",
 // namespace "fast_gpu_asr"), capabilities, output types, shapes and formats; that
 // onShapeChange and enqueue hand TensorRT's descriptors, pointers, field values,
@@ -22,12 +22,15 @@
 #include <vector>
 
 #include "../../include/fga_attention.h"
+#include "../../include/fga_convolution.h"
 
 using namespace nvinfer1;
 
 extern "C" bool initFastGpuAsrParakeetRelativeAttentionPlugin() noexcept;
 extern "C" bool initFastGpuAsrZipformerRelativeAttentionPlugin() noexcept;
 extern "C" bool initFastGpuAsrZipformerAttentionValuePlugin() noexcept;
+extern "C" bool initFastGpuAsrParakeetConvolutionPlugin() noexcept;
+extern "C" bool initFastGpuAsrZipformerConvolutionPlugin() noexcept;
 
 static int g_failures = 0;
 #define CHECK(cond)                                                                   \
@@ -162,6 +165,47 @@ int32_t fga_zipformer_attention_value_enqueue(const fga_tensor_desc* in, const f
     g_last.stream = stream;
     return g_status;
 }
+int32_t fga_parakeet_conformer_convolution_check(const fga_tensor_desc* in, int32_t nin,
+                                                 const fga_tensor_desc* out, int32_t nout) {
+    record("pconv_check", in, nin, out, nout);
+    return g_status;
+}
+size_t fga_parakeet_conformer_convolution_workspace_size(const fga_tensor_desc* in, int32_t nin) {
+    record("pconv_workspace", in, nin, nullptr, 0);
+    return 0;
+}
+int32_t fga_parakeet_conformer_convolution_enqueue(const fga_tensor_desc* in,
+                                                   const fga_tensor_desc* out,
+                                                   const void* const* inputs, void* const* outputs,
+                                                   void* ws, size_t wsb, void* stream) {
+    record("pconv_enqueue", in, 4, out, 1);
+    g_last.inputs = inputs;
+    g_last.outputs = outputs;
+    g_last.workspace = ws;
+    g_last.workspace_bytes = wsb;
+    g_last.stream = stream;
+    return g_status;
+}
+int32_t fga_zipformer_convolution_check(const fga_tensor_desc* in, int32_t nin,
+                                        const fga_tensor_desc* out, int32_t nout) {
+    record("zconv_check", in, nin, out, nout);
+    return g_status;
+}
+size_t fga_zipformer_convolution_workspace_size(const fga_tensor_desc* in, int32_t nin) {
+    record("zconv_workspace", in, nin, nullptr, 0);
+    return 0;
+}
+int32_t fga_zipformer_convolution_enqueue(const fga_tensor_desc* in, const fga_tensor_desc* out,
+                                          const void* const* inputs, void* const* outputs,
+                                          void* ws, size_t wsb, void* stream) {
+    record("zconv_enqueue", in, 4, out, 1);
+    g_last.inputs = inputs;
+    g_last.outputs = outputs;
+    g_last.workspace = ws;
+    g_last.workspace_bytes = wsb;
+    g_last.stream = stream;
+    return g_status;
+}
 }  // extern "C"
 
 // ---- helpers ----------------------------------------------------------------------------
@@ -205,8 +249,12 @@ static void test_registration() {
     CHECK(initFastGpuAsrParakeetRelativeAttentionPlugin());
     CHECK(initFastGpuAsrZipformerRelativeAttentionPlugin());
     CHECK(initFastGpuAsrZipformerAttentionValuePlugin());
+    CHECK(initFastGpuAsrParakeetConvolutionPlugin());
+    CHECK(initFastGpuAsrZipformerConvolutionPlugin());
     for (FakeRegistry* r : {&g_runtime, &g_builder}) {
-        CHECK(r->creators.size() == 3);
+        CHECK(r->creators.size() == 5);
+        CHECK(creator(*r, "parakeet_conformer_convolution") != nullptr);
+        CHECK(creator(*r, "zipformer_convolution") != nullptr);
         CHECK(creator(*r, "parakeet_relative_attention") != nullptr);
         CHECK(creator(*r, "zipformer_relative_attention") != nullptr);
         CHECK(creator(*r, "zipformer_attention_value") != nullptr);
@@ -220,6 +268,8 @@ static void test_registration() {
     CHECK(initFastGpuAsrParakeetRelativeAttentionPlugin());  // idempotent: no re-registration
     CHECK(initFastGpuAsrZipformerRelativeAttentionPlugin());
     CHECK(initFastGpuAsrZipformerAttentionValuePlugin());
+    CHECK(initFastGpuAsrParakeetConvolutionPlugin());
+    CHECK(initFastGpuAsrZipformerConvolutionPlugin());
     CHECK(g_runtime.registrations + g_builder.registrations == before);
     for (auto* r : {&g_runtime, &g_builder})
         for (auto& kv : r->creators) {
@@ -478,12 +528,91 @@ static void test_value_plugin() {
     CHECK(copy != nullptr);
 }
 
+// Both convolution plugins: no fields, x-shaped output of x's type, int32 lengths, the
+// profile's min/opt/max checked through the C ABI, the reference's tactic IDs accepted,
+// exact forwarding with no workspace.
+static void test_convolution_plugin(const char* name, const char* prefix, int32_t tactic) {
+    auto* c = creator(g_runtime, name);
+    CHECK(c->getFieldNames()->nbFields == 0);
+    auto fc0 = fields(nullptr, 0);
+    std::unique_ptr<IPluginV3> p(c->createPlugin("c", &fc0, TensorRTPhase::kBUILD));
+    CHECK(p != nullptr);
+    int32_t k = 9;
+    PluginField extra{"kernel_size", &k, PluginFieldType::kINT32, 1};
+    auto fc1 = fields(&extra, 1);
+    CHECK(c->createPlugin("c", &fc1, TensorRTPhase::kBUILD) == nullptr);
+    CHECK(c->createPlugin("c", nullptr, TensorRTPhase::kBUILD) == nullptr);
+    auto* core = cap<IPluginV3OneCore>(p.get(), PluginCapabilityType::kCORE);
+    auto* build = cap<IPluginV3OneBuild>(p.get(), PluginCapabilityType::kBUILD);
+    auto* rt = cap<IPluginV3OneRuntime>(p.get(), PluginCapabilityType::kRUNTIME);
+    CHECK(std::strcmp(core->getPluginName(), name) == 0);
+    CHECK(std::strcmp(core->getPluginVersion(), "1") == 0);
+    CHECK(std::strcmp(core->getPluginNamespace(), "fast_gpu_asr") == 0);
+    CHECK(std::string(build->getTimingCacheID()).find("impl=fga-sm100a") != std::string::npos);
+    CHECK(rt->setTactic(0) == 0 && rt->setTactic(tactic) == 0 && rt->setTactic(7) != 0);
+
+    DataType ins[4] = {DataType::kHALF, DataType::kINT32, DataType::kHALF, DataType::kHALF}, out;
+    CHECK(build->getOutputDataTypes(&out, 1, ins, 4) == 0 && out == DataType::kHALF);
+    ins[1] = DataType::kHALF;
+    CHECK(build->getOutputDataTypes(&out, 1, ins, 4) != 0);
+    IDimensionExpr n, t, ch, nl, kk, wc, bc;
+    DimsExprs ein[4];
+    ein[0].nbDims = 3; ein[0].d[0] = &n; ein[0].d[1] = &t; ein[0].d[2] = &ch;
+    ein[1].nbDims = 1; ein[1].d[0] = &nl;
+    ein[2].nbDims = 2; ein[2].d[0] = &kk; ein[2].d[1] = &wc;
+    ein[3].nbDims = 1; ein[3].d[0] = &bc;
+    DimsExprs eout[1];
+    IExprBuilder eb;
+    CHECK(build->getOutputShapes(ein, 4, nullptr, 0, eout, 1, eb) == 0);
+    CHECK(eout[0].nbDims == 3 && eout[0].d[0] == &n && eout[0].d[1] == &t && eout[0].d[2] == &ch);
+
+    PluginTensorDesc pin[4] = {desc(DataType::kHALF, {2, 17, 16}), desc(DataType::kINT32, {2}),
+                               desc(DataType::kHALF, {9, 16}), desc(DataType::kHALF, {16})};
+    PluginTensorDesc pout[1] = {desc(DataType::kHALF, {2, 17, 16})};
+    DynamicPluginTensorDesc din[4] = {dyn(pin[0]), dyn(pin[1]), dyn(pin[2]), dyn(pin[3])};
+    DynamicPluginTensorDesc dout[1] = {dyn(pout[0])};
+    DynamicPluginTensorDesc io[5] = {din[0], din[1], din[2], din[3], dout[0]};
+    CHECK(build->supportsFormatCombination(1, io, 4, 1));
+    CHECK(build->supportsFormatCombination(4, io, 4, 1));
+    io[4].desc.type = DataType::kBF16;
+    CHECK(!build->supportsFormatCombination(4, io, 4, 1));
+    g_status = FGA_SUCCESS;
+    CHECK(build->configurePlugin(din, 4, dout, 1) == 0 &&
+          g_last.fn == std::string(prefix) + "_check");
+    g_status = FGA_ERROR_BAD_SHAPE;
+    CHECK(build->configurePlugin(din, 4, dout, 1) != 0);
+    CHECK(rt->onShapeChange(pin, 4, pout, 1) != 0);
+    g_status = FGA_SUCCESS;
+    din[1].desc.type = DataType::kHALF;
+    CHECK(build->configurePlugin(din, 4, dout, 1) != 0);
+    din[1].desc.type = DataType::kINT32;
+    CHECK(build->getWorkspaceSize(din, 4, dout, 1) == 0);
+    CHECK(rt->onShapeChange(pin, 4, pout, 1) == 0);
+    const void* inputs[4] = {reinterpret_cast<void*>(0x10), reinterpret_cast<void*>(0x20),
+                             reinterpret_cast<void*>(0x30), reinterpret_cast<void*>(0x38)};
+    void* outputs[1] = {reinterpret_cast<void*>(0x40)};
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(0x50);
+    CHECK(rt->enqueue(pin, pout, inputs, outputs, nullptr, stream) == 0);
+    CHECK(g_last.fn == std::string(prefix) + "_enqueue" && g_last.stream == stream &&
+          g_last.inputs == inputs && g_last.outputs == outputs && g_last.workspace_bytes == 0);
+    for (int i = 0; i < 4; ++i) CHECK(same(g_last.in[i], pin[i]));
+    CHECK(same(g_last.out[0], pout[0]));
+    g_status = FGA_ERROR_PRIOR_CUDA_ERROR;
+    CHECK(rt->enqueue(pin, pout, inputs, outputs, nullptr, stream) == 1);
+    g_status = FGA_SUCCESS;
+    CHECK(rt->getFieldsToSerialize()->nbFields == 0);
+    std::unique_ptr<IPluginV3> copy(rt->attachToContext(nullptr));
+    CHECK(copy != nullptr);
+}
+
 int main() {
     test_registration();
     test_parakeet_fields();
     test_parakeet_plugin();
     test_weights_plugin();
     test_value_plugin();
+    test_convolution_plugin("parakeet_conformer_convolution", "pconv", 2304);
+    test_convolution_plugin("zipformer_convolution", "zconv", 4096 + 256);
     if (g_failures != 0) {
         std::fprintf(stderr, "%d check(s) failed\n", g_failures);
         return 1;
