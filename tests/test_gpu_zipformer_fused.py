@@ -6,7 +6,8 @@ Checked against the CPU oracle composed of the weights and attention-value resta
 at encoder sizes against this library's two-plugin CUDA path. Tolerances: the outputs
 as the attention-value tests (max-abs fp16 2e-3, bf16 1e-2), since both paths round the
 weights to the I/O type and accumulate in fp32 in different orders; head 0's weights
-bit-identical to the weights entry point's head 0 (the same kernel computes them).
+within the weight tolerance of the weights entry point's head 0 (the two kernels group a
+row's keys differently, so a weight may round to the neighbouring storage value).
 """
 
 from __future__ import annotations
@@ -117,7 +118,12 @@ def test_fused_matches_two_plugin_path_at_encoder_sizes(dtype, batch, length, he
     tol = cases.VALUE_TOL[dtype]
     np.testing.assert_allclose(got[0], ref[0], rtol=tol, atol=tol)
     np.testing.assert_allclose(got[1], ref[1], rtol=tol, atol=tol)
-    np.testing.assert_array_equal(got[2], ref[2])
+    # Head 0's weights: the weights kernel splits a row's keys into 16-key thread groups,
+    # the fused kernel into 32-key groups, so their f16 exponential caches hold values
+    # relative to different running maxima and a weight may round to the neighbouring
+    # storage value; both are within the weight tolerance of the oracle.
+    np.testing.assert_allclose(got[2], ref[2], rtol=cases.WEIGHT_RTOL[dtype],
+                               atol=cases.WEIGHT_ATOL[dtype])
 
 
 def test_fused_repeated_calls_and_streams():
