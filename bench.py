@@ -64,8 +64,10 @@ def parse_args():
     p.add_argument("--batch", type=int, default=None,
                    help="utterances per GPU (default 256; 16 for parakeet_long)")
     p.add_argument("--e2e-steps", type=int, default=2)
-    p.add_argument("--deal", choices=("longest_first", "round_robin"), default="longest_first",
-                   help="ragged workload: how batches are dealt to ranks")
+    p.add_argument("--deal", choices=("dynamic", "longest_first", "round_robin"),
+                   default="dynamic",
+                   help="ragged workload: how batches are dealt to ranks (dynamic: taken one at "
+                        "a time, longest first, from a counter shared through a TCPStore)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -532,9 +534,11 @@ def workload_config(args) -> dict:
 
 # ---- ragged whole-box run (config 5) -------------------------------------------------------
 def ragged_arm(args, world, rank, local):
-    """Length-sorted batches dealt to ranks (longest processing time first by default, or
-    round-robin); per batch the Parakeet stack (24 layers, f16) and the Zipformer stacks
-    (bf16); per-batch outputs of both models gathered to rank 0 at the end.
+    """Length-sorted batches dealt to ranks (by default dynamically: each rank takes the
+    next batch, longest first, from a counter in a TCPStore as soon as it has finished the
+    previous one; or longest processing time first by estimated cost; or round-robin); per
+    batch the Parakeet stack (24 layers, f16) and the Zipformer stacks (bf16); per-batch
+    outputs of both models gathered to rank 0 at the end.
 
     ``value`` = audio seconds of all utterances / max over ranks of the summed batch time
     (CUDA events around each batch's attention calls, host gaps between the launches
@@ -548,18 +552,38 @@ def ragged_arm(args, world, rank, local):
     from fast_gpu_asr_b200 import _lib
     from fast_gpu_asr_b200 import workloads as wl
     from fast_gpu_asr_b200.attention import parakeet_relative_attention
-    from fast_gpu_asr_b200.sharding import (batch_costs, gather_to_rank0, length_sorted_batches,
-                                            shard_longest_first, shard_round_robin)
+    from fast_gpu_asr_b200.sharding import (DynamicDeal, batch_costs, gather_to_rank0,
+                                            length_sorted_batches, shard_longest_first,
+                                            shard_round_robin)
 
     _lib.library()
     stream = torch.cuda.Stream()
     durations = wl.ragged_durations()
     plan = length_sorted_batches(durations, args.batch)
-    if args.deal == "longest_first":
-        assignment = shard_longest_first(batch_costs(plan), world)
+    deal = None
+    if args.deal == "dynamic":
+        import torch.distributed as dist
+
+        if world == 1:
+            store = dist.HashStore()
+        else:
+            store = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"),
+                                  int(os.environ.get("MASTER_PORT", "29500")) + 1, world,
+                                  rank == 0, timeout=timedelta(seconds=120))
+        deal = DynamicDeal(store, np.argsort(-batch_costs(plan), kind="stable"))
+        assignment = None
+        barrier(world)  # every rank's store client is connected before the first take
+
+        def batches():
+            while (b := deal.next()) is not None:
+                yield b
+        mine_iter = batches()
     else:
-        assignment = [shard_round_robin(len(plan), world, r) for r in range(world)]
-    mine = assignment[rank]
+        if args.deal == "longest_first":
+            assignment = shard_longest_first(batch_costs(plan), world)
+        else:
+            assignment = [shard_round_robin(len(plan), world, r) for r in range(world)]
+        mine_iter = iter(assignment[rank])
     warm_p = wl.make_parakeet_layer(2, 64, 8, 128, torch.float16, "cuda", seed=1,
                                     lengths=np.array([64, 33], np.int32))
     warm_z = wl.make_zipformer_layer(2, 64, 192, 4, torch.bfloat16, "cuda", 1,
@@ -583,7 +607,7 @@ def ragged_arm(args, world, rank, local):
             zt = int(wl.zipformer_stack_lengths(in_frames.astype(np.int64), ds).max())
             z_shapes[b.index] += [(len(lens), zt, heads * wl.ZIPFORMER_VALUE_DIM),
                                   (len(lens), zt, 3 * embed // 4)]
-    for idx in mine:
+    for idx in mine_iter:
         b = plan[idx]
         p_lens = np.maximum(1, np.floor(b.lengths / wl.PARAKEET_FRAME_SECONDS)).astype(np.int32)
         t = int(p_lens.max())
@@ -623,6 +647,9 @@ def ragged_arm(args, world, rank, local):
         # The attention outputs of each stack's last layer (self-attention, nonlinear).
         z_outputs[idx] = [t for s in stacks for t in s[3]]
         del players, stacks
+    if deal is not None:
+        assignment = deal.assignment(world)
+    mine = assignment[rank]
     barrier(world)
     max_ms = allreduce_max(kernel_ms, world)
     rank_ms = allgather_floats(kernel_ms, world)

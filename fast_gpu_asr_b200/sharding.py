@@ -14,6 +14,9 @@ benchmark configuration describes for the ragged whole-box run:
   Round-robin over a length-sorted plan gives rank 0 the longest batch of every round,
   which grows the slowest rank's share with the number of ranks; the greedy deal keeps
   the estimated loads within one batch's cost of each other;
+* or dynamically (``DynamicDeal``): the ranks take batches one at a time, longest first,
+  from a shared counter in a key-value store, each as soon as its GPU has finished the
+  previous one, so measured rather than estimated times balance the ranks;
 * each rank runs its batches on its own GPU and stream;
 * at the end the per-batch outputs are gathered to rank 0 with point-to-point sends
   (NCCL over NVLink on GPUs, gloo in the CPU tests), outside the timed kernels.
@@ -79,6 +82,41 @@ def shard_longest_first(costs, world: int) -> list[list[int]]:
         shards[r].append(b)
         loads[r] += costs[b]
     return [sorted(s) for s in shards]
+
+
+class DynamicDeal:
+    """Batches taken one at a time from a counter shared by all ranks.
+
+    ``store`` is a ``torch.distributed`` key-value store reachable by every rank (for
+    example a ``TCPStore`` hosted by rank 0); ``order`` is the sequence in which batches are
+    handed out (longest first: ``np.argsort(-costs, kind="stable")``). Each ``next()`` is one
+    atomic increment of ``key`` in the store and returns the next batch index, or None when
+    every batch is taken; every batch goes to exactly one rank. ``taken`` lists this rank's
+    batches in the order it took them. After the last ``next()``, ``assignment()`` (a
+    collective over the default process group) returns every rank's list for the gather.
+    """
+
+    def __init__(self, store, order, key: str = "fga_deal_next"):
+        self.store = store
+        self.order = [int(b) for b in order]
+        self.key = key
+        self.taken: list[int] = []
+
+    def next(self) -> int | None:
+        i = int(self.store.add(self.key, 1)) - 1
+        if i >= len(self.order):
+            return None
+        self.taken.append(self.order[i])
+        return self.order[i]
+
+    def assignment(self, world: int) -> list[list[int]]:
+        if world == 1:
+            return [sorted(self.taken)]
+        import torch.distributed as dist
+
+        lists: list = [None] * world
+        dist.all_gather_object(lists, sorted(self.taken))
+        return [list(x) for x in lists]
 
 
 def gather_to_rank0(outputs: dict, plan_shapes: dict, world: int, rank: int, device,

@@ -31,23 +31,42 @@ def batch_output(batch_index: int, batch_lengths: np.ndarray) -> np.ndarray:
 
 def run_rank(rank: int, world: int, port: int, lengths: list, batch_size: int, out_path: str,
              deal: str = "round_robin", fail_rank: int = -1):
-    """One rank of the sharded run. ``deal``: "round_robin" or "longest_first" (then every
+    """One rank of the sharded run. ``deal``: "round_robin", "longest_first" (then every
     batch's output is a pair: the weights and their row sums, to exercise multi-tensor
-    gathers). ``fail_rank``: that rank raises after its compute, before the gather; rank 0
+    gathers) or "dynamic" (batches taken from a counter in a TCPStore hosted by rank 0, each
+    after a short sleep standing in for the batch's work; rank 0 records every rank's list in
+    ``out_path`` + ".deal.json"). ``fail_rank``: that rank raises after its compute, before the gather; rank 0
     then records the error its gather raised in ``out_path`` + ".error"."""
     import torch
     import torch.distributed as dist
 
-    from fast_gpu_asr_b200.sharding import (batch_costs, gather_to_rank0, length_sorted_batches,
-                                            shard_longest_first, shard_round_robin)
+    from fast_gpu_asr_b200.sharding import (DynamicDeal, batch_costs, gather_to_rank0,
+                                            length_sorted_batches, shard_longest_first,
+                                            shard_round_robin)
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
     try:
         plan = length_sorted_batches(np.asarray(lengths), batch_size)
+        dynamic = None
         if deal == "longest_first":
             assignment = shard_longest_first(batch_costs(plan), world)
+        elif deal == "dynamic":
+            store = dist.TCPStore("127.0.0.1", port + 1, world, rank == 0,
+                                  timeout=timedelta(seconds=20))
+            costs = batch_costs(plan)
+            dynamic = DynamicDeal(store, np.argsort(-costs, kind="stable"))
+            import time
+
+            while (idx := dynamic.next()) is not None:
+                time.sleep(0.002 * (1 + idx % 3))
+            assignment = dynamic.assignment(world)
+            if rank == 0:
+                import json
+
+                with open(out_path + ".deal.json", "w") as f:
+                    json.dump(assignment, f)
         else:
             assignment = [shard_round_robin(len(plan), world, r) for r in range(world)]
         shapes = {}

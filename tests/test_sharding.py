@@ -109,6 +109,43 @@ def test_gather_with_longest_first_deal_and_tensor_lists(tmp_path, world, count,
         np.testing.assert_allclose(got[f"{b.index}_sum"], w.sum(axis=3), rtol=1e-6)
 
 
+@pytest.mark.parametrize("world,count,batch", [(2, 31, 3), (3, 20, 2)])
+def test_dynamic_deal_takes_every_batch_once_and_gathers(tmp_path, world, count, batch):
+    """Ranks pull batches from a shared counter (longest first): every batch is taken by
+    exactly one rank, every rank takes some, and the gather over that assignment equals the
+    single-process result."""
+    import json
+
+    import torch.multiprocessing as mp
+
+    import dist_worker
+
+    lengths = np.random.default_rng(20 + world).integers(3, 12, size=count).tolist()
+    out = tmp_path / "gathered.npz"
+    mp.start_processes(dist_worker.run_rank,
+                       args=(world, _free_port(), lengths, batch, str(out), "dynamic"),
+                       nprocs=world, join=True, start_method="spawn")
+    plan = length_sorted_batches(np.asarray(lengths), batch)
+    assignment = json.loads((tmp_path / "gathered.npz.deal.json").read_text())
+    taken = sorted(b for r in assignment for b in r)
+    assert taken == list(range(len(plan)))
+    assert all(len(r) > 0 for r in assignment)
+    got = np.load(out)
+    for b in plan:
+        np.testing.assert_array_equal(got[str(b.index)], dist_worker.batch_output(b.index, b.lengths))
+
+
+def test_dynamic_deal_in_one_process():
+    """The counter hands out the order once, then None; with one rank it takes all."""
+    from torch.distributed import HashStore
+
+    from fast_gpu_asr_b200.sharding import DynamicDeal
+
+    deal = DynamicDeal(HashStore(), [3, 0, 2, 1])
+    assert [deal.next() for _ in range(6)] == [3, 0, 2, 1, None, None]
+    assert deal.assignment(1) == [[0, 1, 2, 3]]
+
+
 def test_rank_failing_before_the_gather_is_reported_not_hung(tmp_path):
     """A rank that raises after its compute, before its send: rank 0's gather fails with an
     error well within the process group's timeout (no hang), and it records the error."""
