@@ -607,6 +607,8 @@ def ragged_arm(args, world, rank, local):
             zt = int(wl.zipformer_stack_lengths(in_frames.astype(np.int64), ds).max())
             z_shapes[b.index] += [(len(lens), zt, heads * wl.ZIPFORMER_VALUE_DIM),
                                   (len(lens), zt, 3 * embed // 4)]
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
     for idx in mine_iter:
         b = plan[idx]
         p_lens = np.maximum(1, np.floor(b.lengths / wl.PARAKEET_FRAME_SECONDS)).astype(np.int32)
@@ -647,6 +649,8 @@ def ragged_arm(args, world, rank, local):
         # The attention outputs of each stack's last layer (self-attention, nonlinear).
         z_outputs[idx] = [t for s in stacks for t in s[3]]
         del players, stacks
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - wall0) * 1000.0
     if deal is not None:
         assignment = deal.assignment(world)
     mine = assignment[rank]
@@ -654,6 +658,7 @@ def ragged_arm(args, world, rank, local):
     max_ms = allreduce_max(kernel_ms, world)
     rank_ms = allgather_floats(kernel_ms, world)
     rank_launch_ms = allgather_floats(launch_ms, world)
+    rank_wall_ms = allgather_floats(wall_ms, world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     gathered = gather_to_rank0(outputs, shapes, world, rank, "cuda", torch.float16, assignment)
@@ -674,6 +679,10 @@ def ragged_arm(args, world, rank, local):
                 "batches": len(plan), "batches_per_rank": len(mine), "deal": args.deal,
                 "rank_busy_ms": rank_ms, "rank_busy_spread": max(rank_ms) / max(min(rank_ms), 1e-9),
                 "rank_launch_ms": rank_launch_ms,
+                # Host wall time of each rank's batch loop, input generation included: what
+                # the dynamic deal balances.
+                "rank_wall_ms": rank_wall_ms,
+                "rank_wall_spread": max(rank_wall_ms) / max(min(rank_wall_ms), 1e-9),
                 "gather_wall_s": gather_s, "gathered_bytes": gathered_bytes,
                 "gpu_launches": launches,
                 "variant": _lib.last_kernel_variant()}
@@ -916,12 +925,14 @@ def measure_convolution(args, world, rank, local, peaks, kind: str) -> dict:
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    torch.cuda.nvtx.range_push("fga_timed")
     with torch.cuda.stream(stream):
         start.record(stream)
         for k in range(args.steps):
             step(events[k])
         end.record(stream)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     clocks = sampler.stop() if sampler else None
     barrier(world)
     max_ms = allreduce_max(start.elapsed_time(end), world)
