@@ -34,9 +34,12 @@
 
 #include "fga_kernels.h"
 #include "host_util.h"
+#include "sm100_ptx.cuh"
 
 namespace fga {
 namespace {
+
+using namespace sm100;
 
 constexpr int kConvThreads = 256;
 constexpr int kSlabPairs = 32;  // channel pairs per warp tile (64 channels)
@@ -123,7 +126,10 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
     constexpr int kChunkElems = 16 / static_cast<int>(sizeof(T));
     constexpr bool kWeightsInRegs = kK <= 15;
     constexpr int kRegTaps = kWeightsInRegs ? kK : 1;
-    __shared__ __align__(16) unsigned char s_x[kRows * kRowBytes];
+    // 16-bit types stage the next tile while the current one is computed (two buffers);
+    // fp32 tiles are twice as large and use one.
+    constexpr int kStages = sizeof(T) == 2 ? 2 : 1;
+    __shared__ __align__(16) unsigned char s_x[kStages][kRows * kRowBytes];
     __shared__ __align__(16) unsigned char s_w[kK * kRowBytes];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -136,17 +142,64 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
     const bool vec16 = (channels % kChunkElems) == 0 &&
                        (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 
+    struct Tile {
+        int slab, n, f0;
+    };
+    auto decode = [&](int64_t task) {
+        Tile t;
+        t.slab = static_cast<int>(task / per_slab);
+        const int64_t rem = task - t.slab * per_slab;
+        t.n = static_cast<int>(rem / tiles);
+        t.f0 = static_cast<int>(rem - static_cast<int64_t>(t.n) * tiles) * kBlockFrames;
+        return t;
+    };
+    // The tile's input rows (frames f0 - kPad ...) into buffer `buf`: zeros where a frame is
+    // padded or outside [0, T). 16-byte asynchronous copies (the zeros by a zero source
+    // size), or pair loads and stores when rows are not 16-byte aligned. One commit group.
+    auto stage = [&](int64_t task, int buf) {
+        const Tile t = decode(task);
+        const int requested = __ldg(lens + t.n);
+        const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
+        const T* xb = x + static_cast<int64_t>(t.n) * seq * channels;
+        unsigned char* sx = s_x[buf];
+        if (vec16) {
+            const int c_slab = t.slab * 2 * kSlabPairs;
+            for (int i = tid; i < kRows * kChunks; i += kConvThreads) {
+                const int r = i / kChunks, c = c_slab + (i % kChunks) * kChunkElems;
+                const int fi = t.f0 - kPad + r;
+                const bool valid = static_cast<unsigned>(fi) < static_cast<unsigned>(vl) &&
+                                   c < channels;
+                const T* src = valid ? xb + static_cast<int64_t>(fi) * channels + c : x;
+                cp_async16_zfill(smem_u32(sx + i * 16), src, valid ? 16u : 0u);
+            }
+        } else {
+            for (int i = tid; i < kRows * kSlabPairs; i += kConvThreads) {
+                const int r = i / kSlabPairs, q = t.slab * kSlabPairs + i % kSlabPairs;
+                const int fi = t.f0 - kPad + r;
+                P v = Ops::zero();
+                if (static_cast<unsigned>(fi) < static_cast<unsigned>(vl) && q < npairs)
+                    v = load_pair(xb + static_cast<int64_t>(fi) * channels + 2 * q);
+                *reinterpret_cast<P*>(sx + i * sizeof(P)) = v;
+            }
+        }
+        cp_async_commit();
+    };
+
     P wr[kRegTaps], b0 = Ops::zero();
     int cur_slab = -1;
+    if (kStages == 2 && t_begin < t_end) stage(t_begin, 0);
+    int buf = 0;
     for (int64_t task = t_begin; task < t_end; ++task) {
-        const int slab = static_cast<int>(task / per_slab);
-        const int64_t rem = task - slab * per_slab;
-        const int n = static_cast<int>(rem / tiles);
-        const int f0 = static_cast<int>(rem - static_cast<int64_t>(n) * tiles) * kBlockFrames;
+        const Tile tile = decode(task);
+        const int slab = tile.slab, n = tile.n, f0 = tile.f0;
         const int p = slab * kSlabPairs + lane;
         const bool ok = p < npairs;
         const bool new_slab = slab != cur_slab;
-        __syncthreads();  // the previous tile's rows (and weights) are no longer read
+        // Every warp finished reading the other buffer and the weights (end of the previous
+        // iteration), so they can be refilled.
+        const bool prefetch = kStages == 2 && task + 1 < t_end;
+        if (prefetch) stage(task + 1, buf ^ 1);
+        if (kStages == 1) stage(task, 0);
         if (new_slab) {
             for (int i = tid; i < kK * kSlabPairs; i += kConvThreads) {
                 const int k = i / kSlabPairs, q = slab * kSlabPairs + i % kSlabPairs;
@@ -158,28 +211,8 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         }
         const int requested = __ldg(lens + n);
         const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
-        const T* xb = x + static_cast<int64_t>(n) * seq * channels;
-        const int c_slab = slab * 2 * kSlabPairs;  // first channel of the slab
-        if (vec16) {
-            for (int i = tid; i < kRows * kChunks; i += kConvThreads) {
-                const int r = i / kChunks, c = c_slab + (i % kChunks) * kChunkElems;
-                const int fi = f0 - kPad + r;
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (static_cast<unsigned>(fi) < static_cast<unsigned>(vl) && c < channels)
-                    v = __ldg(reinterpret_cast<const uint4*>(
-                        xb + static_cast<int64_t>(fi) * channels + c));
-                *reinterpret_cast<uint4*>(s_x + i * 16) = v;
-            }
-        } else {
-            for (int i = tid; i < kRows * kSlabPairs; i += kConvThreads) {
-                const int r = i / kSlabPairs, q = slab * kSlabPairs + i % kSlabPairs;
-                const int fi = f0 - kPad + r;
-                P v = Ops::zero();
-                if (static_cast<unsigned>(fi) < static_cast<unsigned>(vl) && q < npairs)
-                    v = load_pair(xb + static_cast<int64_t>(fi) * channels + 2 * q);
-                *reinterpret_cast<P*>(s_x + i * sizeof(P)) = v;
-            }
-        }
+        if (prefetch) cp_async_wait<1>();  // this tile's group is complete
+        else cp_async_wait<0>();
         __syncthreads();
         if constexpr (kWeightsInRegs) {
             if (new_slab) {
@@ -188,9 +221,8 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
                     wr[k] = *reinterpret_cast<const P*>(s_w + k * kRowBytes + lane * sizeof(P));
             }
         }
-        cur_slab = slab;
         const int fw = f0 + warp * kFrames;  // this warp's first output frame
-        const unsigned char* xs = s_x + warp * kFrames * kRowBytes + lane * sizeof(P);
+        const unsigned char* xs = s_x[buf] + warp * kFrames * kRowBytes + lane * sizeof(P);
         P acc[kFrames], win[kFrames];
 #pragma unroll
         for (int j = 0; j < kFrames; ++j) {
@@ -221,7 +253,11 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
                     *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) =
                         activate<T, kAct>(acc[j]);
         }
+        cur_slab = slab;
+        __syncthreads();  // this tile's rows and the weights are read: both may be refilled
+        buf ^= kStages - 1;
     }
+    cp_async_wait<0>();  // nothing left in flight (a block with no tile committed none)
 }
 
 // Any odd tap count: one output frame pair per thread per step, weights read per tap

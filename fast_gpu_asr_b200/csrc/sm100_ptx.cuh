@@ -314,6 +314,23 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[16]) 
 __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&v)[16]) { tmem_st16(taddr, v); }
 __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&v)[8]) { tmem_st8(taddr, v); }
 
+// 16-byte asynchronous global -> shared copy (cp.async, bypassing L1). Bytes past
+// `src_bytes` (0 or 16) are zero-filled: with 0 nothing is read and the destination gets
+// zeros. Completion is tracked by the thread's commit groups.
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst_smem, const void* src,
+                                                 uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's most recent commit groups are pending.
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Named barrier over `count` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
