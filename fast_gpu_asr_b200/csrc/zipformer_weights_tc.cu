@@ -1048,6 +1048,523 @@ zipformer_weights_tc_kernel(const __grid_constant__ CUtensorMap proj_map,
     }
 }
 
+// ---- long rows: 768 < T <= 1536 ----------------------------------------------------------------
+// The exponential cache of zipformer_weights_tc_kernel needs T/2 TMEM columns next to the
+// 128 score columns, so it ends at T = 768. Past it this kernel keeps nothing per key: each
+// query block's score MMAs run twice. Pass 1 reduces every row to its running max and sum;
+// pass 2 recomputes the same logits (the same code, so the same values), writes
+// exp(logit - max) / sum rounded to T, and never caches a key. K of the head stays in shared
+// memory for the pair (T x 64 bytes); Q is loaded per block into two alternating buffers.
+// Pass 2 stores 64-key pieces: the two warps of a TMEM lane quarter each form one 32-key
+// half of the piece into a shared staging tile (two tiles alternate per chunk), meet at a
+// 64-thread named barrier, and write half of the tile's rows each with 16-byte stores
+// aligned to the global addresses, as the short-row kernel does.
+namespace lg {
+constexpr int kMaxT = 1536;
+constexpr int kSub = 2;                     // compute warps per lane quarter: 32-key groups
+constexpr int kGroup = kChunk / kSub;
+constexpr int kComputeWarps = 4 * kSub;
+constexpr int kComputeThreads = 32 * kComputeWarps;
+constexpr int kThreads = kComputeThreads + 32;
+constexpr int kMaxWords = kMaxT / kWord;
+constexpr int kBandFill = kMaxT + kM + 4;
+constexpr int kPlane = 1672;                // >= kBandFill
+constexpr int kCopy = 4 * kPlane + 48;
+constexpr int kPiece = kChunk;
+constexpr int kStageRow = 16 + kPiece * 2;  // 9 x 16 bytes (odd: conflict-free row stores)
+constexpr int kStageTile = 32 * kStageRow;  // one lane quarter's 32 rows
+constexpr uint32_t kTmemCols = 128;         // two 64-key score buffers
+constexpr uint32_t kSmemK = 0;
+constexpr uint32_t kSmemQ = kSmemK + kMaxT * kRowBytes;                // 2 buffers
+constexpr uint32_t kSmemBand = kSmemQ + 2 * kM * kRowBytes;
+constexpr uint32_t kSmemKb = kSmemBand + 4u * kCopy * 2u;              // 2 buffers (pair parity)
+constexpr uint32_t kSmemValid = kSmemKb + 2 * kMaxT * 4;
+constexpr uint32_t kSmemLive = kSmemValid + 2 * kMaxWords * 4;
+constexpr uint32_t kSmemStats = kSmemLive + 2 * 16 * 4;               // [2 subs][rows]
+constexpr uint32_t kSmemStage = (kSmemStats + kSub * kM * 8 + 15u) & ~15u;  // [4][2] tiles
+constexpr uint32_t kSmemBar = kSmemStage + 4 * 2 * kStageTile + 16;
+constexpr uint32_t kBytes = kSmemBar + 128;
+static_assert(kPlane >= kBandFill && kCopy % 64 == 16, "positional band layout");
+static_assert(kBytes <= 227 * 1024, "shared memory budget");
+static_assert(kMaxT / kM <= 16, "block liveness words");
+}  // namespace lg
+
+template <typename T>
+__global__ void __launch_bounds__(lg::kThreads, 1)
+zipformer_weights_long_kernel(const __grid_constant__ CUtensorMap proj_map,
+                              const T* __restrict__ proj, const T* __restrict__ pos,
+                              const uint8_t* __restrict__ mask, T* __restrict__ out, int seq,
+                              int heads, int num_pairs, unsigned int* __restrict__ sched,
+                              uint64_t wait_limit) {
+    // This kernel's sizes (they shadow the short-row kernel's of the same names).
+    constexpr int kMaxT = lg::kMaxT, kSub = lg::kSub, kGroup = lg::kGroup;
+    constexpr int kComputeWarps = lg::kComputeWarps, kComputeThreads = lg::kComputeThreads;
+    constexpr int kThreads = lg::kThreads, kMaxWords = lg::kMaxWords, kBandFill = lg::kBandFill;
+    constexpr int kPlane = lg::kPlane, kCopy = lg::kCopy, kPiece = lg::kPiece;
+    constexpr int kStageRow = lg::kStageRow, kStageTile = lg::kStageTile;
+    constexpr uint32_t kTmemCols = lg::kTmemCols;
+    constexpr uint32_t kSmemK = lg::kSmemK, kSmemQ = lg::kSmemQ, kSmemBand = lg::kSmemBand;
+    constexpr uint32_t kSmemKb = lg::kSmemKb, kSmemValid = lg::kSmemValid, kSmemLive = lg::kSmemLive;
+    constexpr uint32_t kSmemStats = lg::kSmemStats, kSmemStage = lg::kSmemStage;
+    constexpr uint32_t kSmemBar = lg::kSmemBar;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar_k = sbase + kSmemBar;          // K of the pair
+    const uint32_t bar_q = sbase + kSmemBar + 8;      // + 8 * Q buffer
+    const uint32_t bar_full = sbase + kSmemBar + 24;  // + 8 * score buffer
+    const uint32_t bar_free = sbase + kSmemBar + 40;  // + 8 * score buffer
+    const uint32_t bar_drain = sbase + kSmemBar + 56;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 64);
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + kSmemBar + 68);
+    volatile int* next_pair = reinterpret_cast<volatile int*>(smem + kSmemBar + 72);  // [2]
+    uint16_t* band = reinterpret_cast<uint16_t*>(smem + kSmemBand);
+    float2* stats = reinterpret_cast<float2*>(smem + kSmemStats);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const bool control = warp == kComputeWarps;
+    const int qtr = warp & 3;
+    const int sub = warp >> 2;
+    const int q_local = qtr * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(qtr * 32) << 16;
+    const int pdim = heads * (2 * kQd + 4);
+    const int ngroups = (seq + kGroup - 1) / kGroup;
+    const int nwords = (seq + kWord - 1) / kWord;
+    const int nchunks = (seq + kChunk - 1) / kChunk;
+    const int nqb = (seq + kM - 1) / kM;
+
+    if ((sbase & 1023u) != 0) {
+        if (tid == 0) atomicExch(&g_zipformer_tc_error, 2u);
+        return;
+    }
+    if (tid == 0) {
+        mbar_init(bar_k, 1);
+        mbar_init(bar_q, 1);
+        mbar_init(bar_q + 8, 1);
+        mbar_init(bar_full, 1);
+        mbar_init(bar_full + 8, 1);
+        mbar_init(bar_free, kComputeWarps);
+        mbar_init(bar_free + 8, kComputeWarps);
+        mbar_init(bar_drain, 1);
+        *abort = 0u;
+        fence_mbar_init();
+        prefetch_tensormap(&proj_map);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    uint32_t ucount = 0;                  // score-buffer uses (both roles count identically)
+    uint32_t k_phase = 0, q_loads[2] = {0, 0}, q_waits[2] = {0, 0};  // control warp
+    bool k_pending = false;
+    int qi = 0;                           // control warp: live blocks of the run so far
+    int prefetched = -1;                  // control warp: block whose Q is already loading
+    uint32_t pieces = 0;                  // compute warps: pass-2 pieces written so far
+    auto load_q = [&](int b, int pn, int ph) {
+        const int qs = qi & 1;  // the buffer the next live block uses
+        if (lane == 0) {
+            mbar_expect_tx(bar_q + 8 * qs, kM * kRowBytes);
+            tma_load_3d(sbase + kSmemQ + qs * kM * kRowBytes, &proj_map, bar_q + 8 * qs, ph * kQd,
+                        b * kM, pn);
+        }
+        __syncwarp();
+        ++q_loads[qs];
+    };
+    // Waits for the MMA that used score-buffer slot u (the control warp's own commits).
+    auto wait_use = [&](uint32_t u) {
+        return warp_wait(bar_full + 8 * (u & 1), (u >> 1) & 1, abort, wait_limit);
+    };
+
+    if (tid == 0) next_pair[0] = static_cast<int>(atomicAdd(sched, 1u));
+#pragma unroll 1
+    for (int iter = 0;; ++iter) {
+        named_barrier(1, kThreads);
+        const int pair = next_pair[iter & 1];
+        if (pair >= num_pairs) break;
+        if (tid == 0) next_pair[(iter + 1) & 1] = static_cast<int>(atomicAdd(sched, 1u));
+        const int n = pair / heads;
+        const int h = pair - n * heads;
+        const uint8_t* mrow = mask + static_cast<int64_t>(n) * seq;
+        const int buf = iter & 1;
+        float* kb = reinterpret_cast<float*>(smem + kSmemKb) + buf * kMaxT;
+        uint32_t* valid = reinterpret_cast<uint32_t*>(smem + kSmemValid) + buf * kMaxWords;
+        uint32_t* live_q = reinterpret_cast<uint32_t*>(smem + kSmemLive) + buf * 16;
+        if (!control) {
+            for (int wd = warp; wd < nwords; wd += kComputeWarps) {
+                const int k = wd * kWord + lane;
+                const bool v = k < seq && __ldg(mrow + k) == 0;
+                const uint32_t bits = __ballot_sync(0xffffffffu, v);
+                kb[k] = v ? INFINITY : -INFINITY;
+                if (lane == 0) valid[wd] = bits;
+            }
+            for (int b = warp; b < nqb; b += kComputeWarps) {
+                bool any = false;
+#pragma unroll
+                for (int i = 0; i < kM / 32; ++i) {
+                    const int q = b * kM + lane + 32 * i;
+                    any |= q < seq && (q < kHalo || __ldg(mrow + q - kHalo) == 0);
+                }
+                any = __any_sync(0xffffffffu, any);
+                if (lane == 0) live_q[b] = any ? 1u : 0u;
+            }
+        } else if (ucount > 0) {
+            wait_use(ucount - 1);  // K and both Q buffers are free after the last MMA
+        }
+        named_barrier(1, kThreads);  // mask information of this pair is visible
+
+        bool any_valid = false;
+        for (int wd = 0; wd < nwords; ++wd) any_valid |= valid[wd] != 0u;
+        uint32_t live_mask = 0;
+        for (int b = 0; b < nqb; ++b)
+            if (any_valid && live_q[b] != 0u) live_mask |= 1u << b;
+
+        if (control) {
+            // ---- control warp: K of the pair, Q per live block, two rounds of score MMAs ----
+            if (live_mask != 0u && __all_sync(0xffffffffu, *abort == 0u)) {
+                if (lane == 0) {
+                    mbar_expect_tx(bar_k, nqb * kM * kRowBytes);
+                    for (int b = 0; b < nqb; ++b)
+                        tma_load_3d(sbase + kSmemK + b * kM * kRowBytes, &proj_map, bar_k,
+                                    heads * kQd + h * kQd, b * kM, n);
+                }
+                __syncwarp();
+                k_pending = true;
+            }
+            constexpr uint32_t idesc = idesc_f16(Fmt<T>::v, kM, kChunk, 0, 0);
+            prefetched = -1;
+#pragma unroll 1
+            for (int b = 0; b < nqb; ++b) {
+                if (!((live_mask >> b) & 1u)) continue;
+                bool ok = __all_sync(0xffffffffu, *abort == 0u);
+                if (ok && prefetched != b) load_q(b, n, h);  // the pair's first live block
+                const int qs = qi & 1;
+                // The next live block's Q goes to the other buffer, once the MMAs of the block
+                // that used it last have completed.
+                int nb = b + 1;
+                while (nb < nqb && !((live_mask >> nb) & 1u)) ++nb;
+                if (ok && nb < nqb) {
+                    if (ucount > 0) ok = wait_use(ucount - 1);
+                    if (ok) {
+                        ++qi;
+                        load_q(nb, n, h);
+                        --qi;
+                        prefetched = nb;
+                    }
+                }
+                if (ok && k_pending) {
+                    ok = warp_wait(bar_k, k_phase & 1, abort, wait_limit);
+                    if (ok) {
+                        ++k_phase;
+                        k_pending = false;
+                    }
+                }
+                if (ok) {
+                    ok = warp_wait(bar_q + 8 * qs, q_waits[qs] & 1, abort, wait_limit);
+                    if (ok) ++q_waits[qs];
+                }
+                const uint64_t dq = sw64_desc(sbase + kSmemQ + qs * kM * kRowBytes);
+#pragma unroll 1
+                for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll 1
+                    for (int j = 0; j < nchunks; ++j) {
+                        const uint32_t u = ucount++;
+                        const uint32_t sb = u & 1;
+                        bool go = ok && __all_sync(0xffffffffu, *abort == 0u);
+                        if (go && u >= 2)
+                            go = warp_wait(bar_free + 8 * sb, ((u >> 1) - 1) & 1, abort, wait_limit);
+                        if (go) {
+                            tc_fence_after();
+                            if (elect_one()) {
+                                const uint64_t dk = sw64_desc(sbase + kSmemK + j * kChunk * kRowBytes);
+                                const uint32_t d = tmem + sb * kChunk;
+                                umma_f16_ss(d, dq, dk, idesc, 0);
+                                umma_f16_ss(d, dq + 2, dk + 2, idesc, 1);
+                                umma_commit(bar_full + 8 * sb);
+                            }
+                            __syncwarp();
+                        }
+                    }
+                }
+                ++qi;
+            }
+            continue;
+        }
+
+        // ---- compute warps ----
+#pragma unroll 1
+        for (int b = 0; b < nqb; ++b) {
+            const int q0 = b * kM;
+            const int q = q0 + q_local;
+            const bool block_live = (live_mask >> b) & 1u;
+            bool row_live = false;
+            float inv = 0.0f, mlog = 0.0f;
+            uint16_t pq[4] = {0, 0, 0, 0};
+            bool warp_live = false;
+            if (block_live) {
+                named_barrier(2, kComputeThreads);  // previous block's band readers done
+                const int band_lo = seq - 1 - q0 - (kM - 1);
+                const int band_fill = min(kBandFill, kM + ngroups * kGroup + 4);
+                constexpr int kBandIters = (kBandFill + kComputeThreads - 1) / kComputeThreads;
+                uint2 raw_band[kBandIters];
+#pragma unroll
+                for (int it = 0; it < kBandIters; ++it) {
+                    const int i = tid + it * kComputeThreads;
+                    const int rel = band_lo + i;
+                    raw_band[it] = make_uint2(0u, 0u);
+                    if (i < band_fill && i < seq + kM - 1 && rel >= 0 && rel < 2 * seq - 1)
+                        raw_band[it] = __ldg(reinterpret_cast<const uint2*>(
+                            pos + (static_cast<int64_t>(rel) * heads + h) * 4));
+                }
+                uint2 raw_pq = make_uint2(0u, 0u);
+                uint8_t halo_mask = 0;
+                if (q < seq) {
+                    raw_pq = __ldg(reinterpret_cast<const uint2*>(
+                        proj + (static_cast<int64_t>(n) * seq + q) * pdim + 2 * heads * kQd + h * 4));
+                    if (q >= kHalo) halo_mask = __ldg(mrow + q - kHalo);
+                }
+#pragma unroll
+                for (int it = 0; it < kBandIters; ++it) {
+                    const int i = tid + it * kComputeThreads;
+                    if (i >= band_fill) break;
+                    const uint2 raw = raw_band[it];
+                    const uint16_t v[4] = {static_cast<uint16_t>(raw.x & 0xFFFFu),
+                                           static_cast<uint16_t>(raw.x >> 16),
+                                           static_cast<uint16_t>(raw.y & 0xFFFFu),
+                                           static_cast<uint16_t>(raw.y >> 16)};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (i >= c) {
+#pragma unroll
+                            for (int pl = 0; pl < 4; ++pl)
+                                band[c * kCopy + pl * kPlane + i - c] = v[pl];
+                        }
+                    }
+                }
+                if (q < seq) {
+                    pq[0] = static_cast<uint16_t>(raw_pq.x & 0xFFFFu);
+                    pq[1] = static_cast<uint16_t>(raw_pq.x >> 16);
+                    pq[2] = static_cast<uint16_t>(raw_pq.y & 0xFFFFu);
+                    pq[3] = static_cast<uint16_t>(raw_pq.y >> 16);
+                    row_live = halo_mask == 0;
+                }
+                warp_live = __any_sync(0xffffffffu, row_live);
+                named_barrier(3, kComputeThreads);  // band complete
+                tc_fence_after();
+            }
+            const int prow = (kM - 1) - q_local;
+            // Logits of this thread's 32-key group g from the content scores r (the same code
+            // in both passes, so both passes see the same values).
+            auto logits = [&](int g, uint32_t vb, const uint32_t (&r)[32], float (&s)[32]) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float2 f = round_pair<T>(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                    s[2 * i] = f.x;
+                    s[2 * i + 1] = f.y;
+                }
+                const int b0 = prow + g * kGroup;
+                const int cpy = b0 & 3;
+                const uint16_t* bp = band + cpy * kCopy + (b0 - cpy);
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+#pragma unroll
+                    for (int pl = 0; pl < 4; ++pl) {
+                        const uint2 v = *reinterpret_cast<const uint2*>(bp + pl * kPlane + 4 * t);
+                        fma_pair<T>(s[4 * t], s[4 * t + 1], pq[pl], v.x);
+                        fma_pair<T>(s[4 * t + 2], s[4 * t + 3], pq[pl], v.y);
+                    }
+                }
+                if (vb != 0xffffffffu) {
+                    const float* kp = kb + g * kGroup;
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+                        const float4 m4 = *reinterpret_cast<const float4*>(kp + 4 * t);
+                        s[4 * t] = fminf(s[4 * t], m4.x);
+                        s[4 * t + 1] = fminf(s[4 * t + 1], m4.y);
+                        s[4 * t + 2] = fminf(s[4 * t + 2], m4.z);
+                        s[4 * t + 3] = fminf(s[4 * t + 3], m4.w);
+                    }
+                }
+            };
+            // The content scores of use u for this thread's group; false: no math needed.
+            auto scores = [&](uint32_t u, bool math, uint32_t (&r)[32]) {
+                const uint32_t sb = u & 1;
+                const bool ok = warp_wait(bar_full + 8 * sb, (u >> 1) & 1, abort, wait_limit);
+                if (ok && math) {
+                    tmem_ld32(tmem + lane_off + sb * kChunk + sub * kGroup, r);
+                    tmem_wait_ld();
+                    reg_fence(r);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_free + 8 * sb);
+                return ok && math;
+            };
+
+            if (block_live) {
+                // ---- pass 1: running max and sum of every row ----
+                const float2 l2e = make_float2(kLog2e, kLog2e);
+                float m_run = -INFINITY, l_run = 0.0f;
+#pragma unroll 1
+                for (int j = 0; j < nchunks; ++j) {
+                    const int g = 2 * j + sub;
+                    const uint32_t vb = g < ngroups ? valid[g] : 0u;
+                    uint32_t r[32];
+                    if (!scores(ucount + j, warp_live && vb != 0u, r)) continue;
+                    float s[32];
+                    logits(g, vb, r, s);
+                    float m4[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(s[i], s[i + 4], s[i + 8]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[i + 12], s[i + 16]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) m4[i] = fmax3(m4[i], s[i + 20], s[i + 24]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) m4[i] = fmaxf(m4[i], s[i + 28]);
+                    const float m_new = fmaxf(m_run, fmaxf(fmax3(m4[0], m4[1], m4[2]), m4[3]));
+                    const float mb = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
+                    const float2 nb = make_float2(-mb, -mb);
+                    float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                                     make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), l2e, nb);
+                        acc[i & 3] = __fadd2_rn(acc[i & 3], make_float2(fast_exp2(x.x), fast_exp2(x.y)));
+                    }
+                    const float2 accs =
+                        __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+                    const float alpha = m_run == m_new ? 1.0f : fast_exp2((m_run - m_new) * kLog2e);
+                    l_run = fmaf(l_run, alpha, accs.x + accs.y);
+                    m_run = m_new;
+                }
+                ucount += nchunks;
+                stats[sub * kM + q_local] = make_float2(m_run, row_live ? l_run : 0.0f);
+                named_barrier(4, kComputeThreads);  // both sub-slots' statistics written
+                float m_fin = -INFINITY, l_fin = 0.0f;
+#pragma unroll
+                for (int s2 = 0; s2 < kSub; ++s2) m_fin = fmaxf(m_fin, stats[s2 * kM + q_local].x);
+#pragma unroll
+                for (int s2 = 0; s2 < kSub; ++s2) {
+                    const float2 st = stats[s2 * kM + q_local];
+                    l_fin += st.y * (st.x == m_fin ? 1.0f : fast_exp2((st.x - m_fin) * kLog2e));
+                }
+                inv = l_fin > 0.0f ? 1.0f / l_fin : 0.0f;
+                row_live = row_live && inv > 0.0f;
+                mlog = m_fin == -INFINITY ? 0.0f : m_fin * kLog2e;
+                named_barrier(4, kComputeThreads);  // statistics read before the next block
+            }
+
+            // ---- pass 2: recompute the logits, normalise, write 64-key pieces ----
+            const int rows_here = min(32, seq - (q0 + qtr * 32));
+            const int64_t e_base =
+                (static_cast<int64_t>(n * heads + h) * seq + q0 + qtr * 32) * seq;
+            uint4 carry = make_uint4(0u, 0u, 0u, 0u);  // sub-slot 1: last 8 keys of the previous piece
+#pragma unroll 1
+            for (int j = 0; j < nchunks; ++j, ++pieces) {
+                const int k0 = j * kPiece;
+                const int g = 2 * j + sub;
+                const uint32_t vb = g < ngroups ? valid[g] : 0u;
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) w[i] = 0u;
+                if (block_live) {
+                    uint32_t r[32];
+                    if (scores(ucount + j, warp_live && vb != 0u, r) && row_live) {
+                        float s[32];
+                        logits(g, vb, r, s);
+                        const float2 l2e = make_float2(kLog2e, kLog2e);
+                        const float2 nb = make_float2(-mlog, -mlog);
+                        const float2 sc = make_float2(inv, inv);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), l2e, nb);
+                            const float2 e = __fmul2_rn(make_float2(fast_exp2(x.x), fast_exp2(x.y)), sc);
+                            w[i] = pack_pair<T>(e.x, e.y);
+                        }
+                    }
+                }
+                // Stage this warp's half of the piece (sub-slot 1 adds the carry), then write
+                // half of the quarter's rows each.
+                // The two tiles alternate over every piece of the run (blocks included), so a
+                // tile is refilled only after both warps have passed the next piece's barrier.
+                uint8_t* tile = smem + kSmemStage + (qtr * 2 + (pieces & 1u)) * kStageTile;
+                uint8_t* srow = tile + lane * kStageRow;
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    *reinterpret_cast<uint4*>(srow + 16 + 64 * sub + 16 * i) =
+                        make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                if (sub == 1) {
+                    *reinterpret_cast<uint4*>(srow) = carry;
+                    carry = make_uint4(w[12], w[13], w[14], w[15]);
+                }
+                named_barrier(5 + qtr, 64);  // both halves of the quarter's piece are staged
+#pragma unroll
+                for (int it = 4 * sub; it < 4 * sub + 4; ++it) {
+                    const int row = it * 4 + (lane >> 3);
+                    const int m = lane & 7;
+                    if (row < rows_here) {
+                        const int64_t e_row = e_base + static_cast<int64_t>(row) * seq;
+                        const int d = static_cast<int>(e_row & 7);
+                        const int lo = k0 - d + 8 * m;
+                        const uint8_t* sr = tile + row * kStageRow;
+                        if (lo >= 0 && lo + 8 <= seq) {
+                            const int s0 = 8 - d + 8 * m;
+                            const uint32_t* wp = reinterpret_cast<const uint32_t*>(sr) + (s0 >> 1);
+                            const uint32_t a0 = wp[0], a1 = wp[1], a2 = wp[2], a3 = wp[3], a4 = wp[4];
+                            const uint32_t sel = (s0 & 1) ? 0x5432u : 0x3210u;
+                            *reinterpret_cast<uint4*>(out + e_row + lo) =
+                                make_uint4(__byte_perm(a0, a1, sel), __byte_perm(a1, a2, sel),
+                                           __byte_perm(a2, a3, sel), __byte_perm(a3, a4, sel));
+                        } else if (lo + 8 > 0 && lo < seq) {
+                            const T* se = reinterpret_cast<const T*>(sr);
+                            for (int k = max(lo, 0); k < min(lo + 8, seq); ++k)
+                                out[e_row + k] = se[k - k0 + 8];
+                        }
+                    }
+                }
+                if (j + 1 == nchunks && lane < 16 && 16 * sub + lane < rows_here) {
+                    // Keys after the last slot of the row (slot m = 8, always partial).
+                    const int row = 16 * sub + lane;
+                    const int64_t e_row = e_base + static_cast<int64_t>(row) * seq;
+                    const int d = static_cast<int>(e_row & 7);
+                    const int lo = k0 - d + kPiece;
+                    const T* se = reinterpret_cast<const T*>(tile + row * kStageRow);
+                    for (int k = max(lo, 0); k < min(lo + 8, seq); ++k) out[e_row + k] = se[k - k0 + 8];
+                }
+            }
+            if (block_live) ucount += nchunks;
+            tc_fence_before();
+        }
+    }
+
+    // Teardown, with the default time limit whatever the launch's: the control warp waits
+    // for every MMA it issued and for loads still in flight (only after an abort).
+    if (control) {
+        bool ok = true;
+        if (elect_one()) {
+            umma_commit(bar_drain);
+            ok = mbar_wait(bar_drain, 0);
+        }
+        __syncwarp();
+        if (k_pending) ok = mbar_wait(bar_k, k_phase & 1) && ok;
+        for (int s2 = 0; s2 < 2; ++s2)
+            if (q_loads[s2] > q_waits[s2]) ok = mbar_wait(bar_q + 8 * s2, q_waits[s2] & 1) && ok;
+        if (!ok) atomicExch(&g_zipformer_tc_error, 1u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
 // ---- host side ------------------------------------------------------------------------------
 CUtensorMapDataType map_type(int32_t dtype) {
     return dtype == FGA_HALF ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -1116,6 +1633,30 @@ cudaError_t weights_tc_typed(const ZipformerWeightsProblem& p, cudaStream_t stre
 }
 
 template <typename T>
+cudaError_t weights_long_typed(const ZipformerWeightsProblem& p, cudaStream_t stream) {
+    EncodeTiledFn encode = encode_fn();
+    if (encode == nullptr) return cudaErrorNotSupported;
+    CUtensorMap map;
+    if (!encode_proj_map(encode, &map, p.projection, p.dtype, p.batch, p.length, p.heads))
+        return cudaErrorNotSupported;
+    static SmemAttr attr;
+    if (cudaError_t e = attr.ensure(reinterpret_cast<const void*>(zipformer_weights_long_kernel<T>),
+                                    static_cast<int>(lg::kBytes));
+        e != cudaSuccess)
+        return e;
+    const int64_t pairs = static_cast<int64_t>(p.batch) * p.heads;
+    const int sms = sm_count();
+    if (sms <= 0) return cudaErrorNotSupported;
+    const int grid = static_cast<int>(pairs < sms ? pairs : sms);
+    if (cudaError_t e = zero_counter(p.sched, stream); e != cudaSuccess) return e;
+    zipformer_weights_long_kernel<T><<<grid, lg::kThreads, lg::kBytes, stream>>>(
+        map, static_cast<const T*>(p.projection), static_cast<const T*>(p.position), p.mask,
+        static_cast<T*>(p.weights), p.length, p.heads, static_cast<int>(pairs), p.sched,
+        wait_limit_ns());
+    return cudaGetLastError();
+}
+
+template <typename T>
 cudaError_t fused_tc_typed(const ZipformerFusedProblem& p, cudaStream_t stream) {
     EncodeTiledFn encode = encode_fn();
     if (encode == nullptr) return cudaErrorNotSupported;
@@ -1177,7 +1718,7 @@ cudaError_t no_workspace_scratch(void** ptr) {
 cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem& p, cudaStream_t stream) {
     if (p.query_dim != kQd || (p.dtype != FGA_HALF && p.dtype != FGA_BF16))
         return cudaErrorNotSupported;
-    if (p.length > kMaxT || p.length < 1) return cudaErrorNotSupported;
+    if (p.length > lg::kMaxT || p.length < 1) return cudaErrorNotSupported;
     if (static_cast<int64_t>(p.batch) * p.heads > (1ll << 30)) return cudaErrorNotSupported;
     // TMA needs 16-byte row strides (H * (2*32+4) * 2 bytes = 136 H) and a 16-byte aligned
     // base; the aligned row writes need a 16-byte aligned output.
@@ -1186,6 +1727,9 @@ cudaError_t launch_zipformer_weights_tc(const ZipformerWeightsProblem& p, cudaSt
         (reinterpret_cast<uintptr_t>(p.weights) & 15u) != 0 ||
         (reinterpret_cast<uintptr_t>(p.position) & 7u) != 0)
         return cudaErrorNotSupported;
+    if (p.length > kMaxT)  // past the exponential cache: two rounds of score MMAs
+        return p.dtype == FGA_HALF ? weights_long_typed<__half>(p, stream)
+                                   : weights_long_typed<__nv_bfloat16>(p, stream);
     return p.dtype == FGA_HALF ? weights_tc_typed<__half>(p, stream)
                                : weights_tc_typed<__nv_bfloat16>(p, stream);
 }

@@ -98,6 +98,46 @@ def test_weights_known_answers(dtype, name, x, expected):
     assert_weights_match(x, dtype, actual)
 
 
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("batch,length,lengths", [(3, 769, (769, 400, 5)), (2, 875, (875, 870)),
+                                                  (4, 800, (800, 9, 700, 1)),
+                                                  (2, 1536, (1536, 1100))])
+def test_weights_long_rows_on_tensor_cores(dtype, batch, length, lengths):
+    """768 < T <= 1536 runs the two-round tensor-core kernel (no exponential cache): every
+    element against the oracle, lengths from 1 to T (dead query blocks, the halo)."""
+    x = cases.zipformer_inputs(batch, length, lengths=list(lengths))
+    assert_weights_match(x, dtype)
+    assert _lib.last_kernel_variant() == "tcgen05"
+
+
+def test_weights_long_rows_ragged_batch_structure():
+    """The ragged run's longest batch shape (utterances near 35 s: stack-1 T = 875) with 32
+    utterances and 4 heads: live rows sum to 1, padded rows and keys are zero, and two
+    sampled utterances match the oracle."""
+    from fast_gpu_asr_b200.workloads import make_zipformer_layer
+
+    lengths = np.random.default_rng(5).integers(700, 876, size=32)
+    lengths[0] = 875
+    layer = make_zipformer_layer(32, 875, 192, 4, torch.bfloat16, "cuda", 9, lengths)
+    w = zipformer_relative_attention(layer.projection, layer.position, layer.mask)
+    torch.cuda.synchronize()
+    assert _lib.last_kernel_variant() == "tcgen05"
+    sums = w.float().sum(dim=3)
+    t = torch.arange(875, device="cuda")
+    live = t[None, :] < (torch.as_tensor(lengths, device="cuda")[:, None] + 7)
+    assert torch.allclose(sums[live[:, None, :].expand_as(sums)], torch.ones(()), atol=2e-2)
+    assert (sums[~live[:, None, :].expand_as(sums)] == 0).all()
+    for b in (0, 31):
+        x = dict(projection=layer.projection[b : b + 1].float().cpu().numpy(),
+                 position=layer.position.float().cpu().numpy(),
+                 mask=layer.mask[b : b + 1].cpu().numpy())
+        cases.assert_zipformer_weights_match(w[b : b + 1].float().cpu().numpy(),
+                                             oracle_weights(x["projection"], x["position"],
+                                                            x["mask"], "bfloat16"),
+                                             x["projection"], x["position"], x["mask"],
+                                             "bfloat16", 4)
+
+
 @pytest.mark.parametrize("length,padded", [(385, False), (65, True), (1025, True)])
 def test_weights_uniform_masks(length, padded):
     x = cases.zipformer_inputs(1, length)
