@@ -1,5 +1,7 @@
 // Zipformer relative-position attention weights on tcgen05 tensor cores (f16/bf16, query
-// head dim 32, T <= 768).
+// head dim 32): T <= 768 with an exponential cache in TMEM (zipformer_weights_tc_kernel,
+// below); 768 < T <= 1536 recomputing the scores (zipformer_weights_long_kernel, at the
+// end of the file).
 //
 // W[n, h, q, k] = softmax_k( round_T(Q[q] . K[k]) + sum_i pq[q,i] * pos[T-1-q+k, i] ),
 // masked keys excluded, written as the I/O dtype T in the NHTT layout.
