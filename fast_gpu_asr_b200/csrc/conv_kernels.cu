@@ -31,6 +31,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <type_traits>
 
 #include "fga_kernels.h"
 #include "host_util.h"
@@ -92,6 +93,50 @@ __device__ __forceinline__ typename PairOps<T>::P activate(typename PairOps<T>::
     else return PairOps<T>::from_float2(swoosh_r(f.x), swoosh_r(f.y));
 }
 
+// bf16 activation table. The activation's input is the sum rounded to bf16 and its output
+// is rounded to bf16, so for bf16 it is a function of 16 bits. The table holds it for
+// every bf16 of magnitude in [2^-12, 2^8) (20 binades x 128 significands, both signs):
+// 5120 entries, 10 KB of shared memory per block, computed by the same `silu` / `swoosh_r`
+// code the direct path runs, so a looked-up value equals the computed one bit for bit.
+// Inputs outside the range (zeros, tiny and large magnitudes, inf, NaN) are computed.
+//
+// Each device holds one copy per activation in global memory, built by the first launch
+// that finds its ready flag clear: every block of that launch computes the table itself,
+// writes it to shared memory and to the global copy, and publishes the flag with a release
+// store after a fence. Later blocks that read the flag set (acquire) copy the 10 KB from
+// L2 instead. Concurrent builders write identical values.
+constexpr uint32_t kLutExpLo = 115;                   // biased exponent of 2^-12
+constexpr uint32_t kLutExps = 20;                     // through 2^7 (|v| < 2^8)
+constexpr uint32_t kLutBase = kLutExpLo << 7;         // first magnitude pattern
+constexpr uint32_t kLutSpan = kLutExps << 7;          // magnitudes per sign
+constexpr int kLutEntries = 2 * static_cast<int>(kLutSpan);
+constexpr int kLutBytes = kLutEntries * 2;
+
+__device__ __align__(16) uint16_t g_bf16_act_lut[2][kLutEntries];
+__device__ unsigned int g_bf16_act_lut_ready[2];
+
+template <int kAct> __device__ __forceinline__ uint16_t lut_entry(int i) {
+    const uint32_t sign = static_cast<uint32_t>(i) >= kLutSpan ? 0x8000u : 0u;
+    const uint32_t bits = sign | (kLutBase + static_cast<uint32_t>(i) % kLutSpan);
+    const float v = __uint_as_float(bits << 16);
+    const float a = kAct == kSilu ? silu(v) : swoosh_r(v);
+    return __bfloat16_as_ushort(__float2bfloat16_rn(a));
+}
+
+template <int kAct>
+__device__ __forceinline__ __nv_bfloat162 activate_lut(__nv_bfloat162 v, const uint16_t* lut) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(&v);
+    const uint32_t o0 = (w & 0x7FFFu) - kLutBase;  // wraps above the span below the range
+    const uint32_t o1 = ((w >> 16) & 0x7FFFu) - kLutBase;
+    if (o0 < kLutSpan && o1 < kLutSpan) {
+        const uint32_t lo = lut[o0 + ((w >> 15) & 1u) * kLutSpan];
+        const uint32_t hi = lut[o1 + (w >> 31) * kLutSpan];
+        const uint32_t r = lo | (hi << 16);
+        return *reinterpret_cast<const __nv_bfloat162*>(&r);
+    }
+    return activate<__nv_bfloat16, kAct>(v);
+}
+
 template <typename T> __device__ __forceinline__ typename PairOps<T>::P load_pair(const T* p) {
     return *reinterpret_cast<const typename PairOps<T>::P*>(p);
 }
@@ -110,8 +155,10 @@ template <typename T> __host__ __device__ constexpr int frames_per_tile() { retu
 // that slides by one row per tap (one shared-memory load per tap) and every accumulator
 // receives its taps in tap order. Weights up to 15 taps stay in registers for the block's
 // run of tiles of one slab; longer kernels read each tap's weight from shared memory.
+// Four blocks per SM (64 registers): the kernel is issue-bound, and at three blocks the
+// kernel-15 instantiations (weights in registers) ran slower.
 template <typename T, int kK, int kAct, bool kSkip>
-__global__ void __launch_bounds__(kConvThreads)
+__global__ void __launch_bounds__(kConvThreads, 4)
 depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
                       const T* __restrict__ w, const T* __restrict__ bias, T* __restrict__ y,
                       int batch, int seq, int channels, int tiles, int64_t tasks) {
@@ -129,8 +176,11 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
     // 16-bit types stage the next tile while the current one is computed (two buffers);
     // fp32 tiles are twice as large and use one.
     constexpr int kStages = sizeof(T) == 2 ? 2 : 1;
+    // bf16 looks its activation up in a table (dynamic shared memory, kLutBytes).
+    constexpr bool kLut = std::is_same<T, __nv_bfloat16>::value;
     __shared__ __align__(16) unsigned char s_x[kStages][kRows * kRowBytes];
     __shared__ __align__(16) unsigned char s_w[kK * kRowBytes];
+    extern __shared__ __align__(16) unsigned char s_dyn[];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int npairs = channels / 2;
@@ -142,6 +192,8 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
     const bool vec16 = (channels % kChunkElems) == 0 &&
                        (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 
+    // A task's (slab, utterance, frame tile): the block's first task is decoded once, each
+    // next one is its predecessor advanced by one tile (no division per tile).
     struct Tile {
         int slab, n, f0;
     };
@@ -153,11 +205,21 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         t.f0 = static_cast<int>(rem - static_cast<int64_t>(t.n) * tiles) * kBlockFrames;
         return t;
     };
+    auto advance = [&](Tile t) {
+        t.f0 += kBlockFrames;
+        if (t.f0 >= tiles * kBlockFrames) {
+            t.f0 = 0;
+            if (++t.n == batch) {
+                t.n = 0;
+                ++t.slab;
+            }
+        }
+        return t;
+    };
     // The tile's input rows (frames f0 - kPad ...) into buffer `buf`: zeros where a frame is
     // padded or outside [0, T). 16-byte asynchronous copies (the zeros by a zero source
     // size), or pair loads and stores when rows are not 16-byte aligned. One commit group.
-    auto stage = [&](int64_t task, int buf) {
-        const Tile t = decode(task);
+    auto stage = [&](const Tile& t, int buf) {
         const int requested = __ldg(lens + t.n);
         const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
         const T* xb = x + static_cast<int64_t>(t.n) * seq * channels;
@@ -187,10 +249,34 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
 
     P wr[kRegTaps], b0 = Ops::zero();
     int cur_slab = -1;
-    if (kStages == 2 && t_begin < t_end) stage(t_begin, 0);
+    Tile cur = t_begin < t_end ? decode(t_begin) : Tile{0, 0, 0};
+    if (kStages == 2 && t_begin < t_end) stage(cur, 0);
+    uint16_t* const lut = reinterpret_cast<uint16_t*>(s_dyn);
+    if constexpr (kLut) {
+        // Fill the activation table (under the first tile's copies).
+        __shared__ unsigned int s_lut_ready;
+        if (tid == 0) s_lut_ready = ld_acquire_gpu(&g_bf16_act_lut_ready[kAct]);
+        __syncthreads();
+        const bool ready = s_lut_ready != 0u;
+        if (ready) {
+            const uint4* src = reinterpret_cast<const uint4*>(g_bf16_act_lut[kAct]);
+            for (int i = tid; i < kLutBytes / 16; i += kConvThreads)
+                reinterpret_cast<uint4*>(lut)[i] = __ldcg(src + i);
+        } else {
+            for (int i = tid; i < kLutEntries; i += kConvThreads) {
+                const uint16_t e = lut_entry<kAct>(i);
+                lut[i] = e;
+                g_bf16_act_lut[kAct][i] = e;
+            }
+            __threadfence();
+        }
+        __syncthreads();
+        if (!ready && tid == 0) st_release_gpu(&g_bf16_act_lut_ready[kAct], 1u);
+    }
     int buf = 0;
     for (int64_t task = t_begin; task < t_end; ++task) {
-        const Tile tile = decode(task);
+        const Tile tile = cur;
+        const Tile next = advance(cur);
         const int slab = tile.slab, n = tile.n, f0 = tile.f0;
         const int p = slab * kSlabPairs + lane;
         const bool ok = p < npairs;
@@ -198,8 +284,8 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         // Every warp finished reading the other buffer and the weights (end of the previous
         // iteration), so they can be refilled.
         const bool prefetch = kStages == 2 && task + 1 < t_end;
-        if (prefetch) stage(task + 1, buf ^ 1);
-        if (kStages == 1) stage(task, 0);
+        if (prefetch) stage(next, buf ^ 1);
+        if (kStages == 1) stage(tile, 0);
         if (new_slab) {
             for (int i = tid; i < kK * kSlabPairs; i += kConvThreads) {
                 const int k = i / kSlabPairs, q = slab * kSlabPairs + i % kSlabPairs;
@@ -249,11 +335,15 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
             T* yp = y + (static_cast<int64_t>(n) * seq + fw) * channels + 2 * p;
 #pragma unroll
             for (int j = 0; j < kFrames; ++j)
-                if (fw + j < seq)
-                    *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) =
-                        activate<T, kAct>(acc[j]);
+                if (fw + j < seq) {
+                    P out;
+                    if constexpr (kLut) out = activate_lut<kAct>(acc[j], lut);
+                    else out = activate<T, kAct>(acc[j]);
+                    *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) = out;
+                }
         }
         cur_slab = slab;
+        cur = next;
         __syncthreads();  // this tile's rows and the weights are read: both may be refilled
         buf ^= kStages - 1;
     }
@@ -293,15 +383,17 @@ depthwise_conv_any_kernel(const T* __restrict__ x, const int32_t* __restrict__ l
     }
 }
 
-// Resident blocks per SM of a kernel, looked up once per (kernel, device).
-template <typename Kernel> int blocks_per_sm(Kernel kernel) {
+// Resident blocks per SM of a kernel with `dyn_smem` bytes of dynamic shared memory,
+// looked up once per (kernel, device).
+template <typename Kernel> int blocks_per_sm(Kernel kernel, int dyn_smem = 0) {
     static std::atomic<int> cache[kMaxCachedDevices];
     const int dev = current_device();
     if (dev >= 0 && dev < kMaxCachedDevices) {
         if (const int v = cache[dev].load(std::memory_order_relaxed)) return v;
     }
     int v = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kConvThreads, 0) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kConvThreads, dyn_smem) !=
+            cudaSuccess ||
         v < 1)
         v = 1;
     if (dev >= 0 && dev < kMaxCachedDevices) cache[dev].store(v, std::memory_order_relaxed);
@@ -317,9 +409,15 @@ cudaError_t launch_fixed(const ConvolutionProblem& p, cudaStream_t stream) {
     auto kernel = depthwise_conv_kernel<T, kK, kAct, kSkip>;
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
-    int64_t grid = static_cast<int64_t>(sms) * blocks_per_sm(kernel);
+    constexpr int kDyn = std::is_same<T, __nv_bfloat16>::value ? kLutBytes : 0;
+    if constexpr (kDyn > 0) {
+        static SmemAttr attr;
+        const cudaError_t e = attr.ensure(reinterpret_cast<const void*>(kernel), kDyn);
+        if (e != cudaSuccess) return e;
+    }
+    int64_t grid = static_cast<int64_t>(sms) * blocks_per_sm(kernel, kDyn);
     if (grid > tasks) grid = tasks;
-    kernel<<<static_cast<unsigned>(grid), kConvThreads, 0, stream>>>(
+    kernel<<<static_cast<unsigned>(grid), kConvThreads, kDyn, stream>>>(
         static_cast<const T*>(p.x), p.valid_lengths, static_cast<const T*>(p.weight),
         static_cast<const T*>(p.bias), static_cast<T*>(p.output), p.batch, p.length, p.channels,
         tiles, tasks);

@@ -59,8 +59,11 @@ def run_rank(rank: int, world: int, port: int, lengths: list, batch_size: int, o
             dynamic = DynamicDeal(store, np.argsort(-costs, kind="stable"))
             import time
 
+            # Every rank starts pulling together, and each batch takes a few milliseconds of
+            # "work", so no rank can drain the counter before the others begin.
+            dist.barrier()
             while (idx := dynamic.next()) is not None:
-                time.sleep(0.002 * (1 + idx % 3))
+                time.sleep(0.01 * (1 + idx % 3))
             assignment = dynamic.assignment(world)
             if rank == 0:
                 import json

@@ -123,6 +123,40 @@ def test_activation_extremes(kind, dtype):
     assert_matches(got, x, [7], w, b, kind, dtype)
 
 
+@pytest.mark.parametrize("dtype", ("bfloat16", "float16"))
+@pytest.mark.parametrize("kind", list(KINDS))
+def test_activation_table_equals_direct_evaluation(kind, dtype):
+    """The bf16 kernels for K = 9, 15, 31 look the activation up in a table; the kernel for
+    other K evaluates it (f16 evaluates it in both). With zero weights the sum is the bias,
+    so a bias holding all 65536 patterns of the type (one per channel) drives every table
+    entry and every out-of-range input (zeros, subnormals, large magnitudes, infinities,
+    NaNs) through both paths; the outputs must agree bit for bit. Run twice: the first call
+    may build the device's table, the second copies it."""
+    op, _ = KINDS[kind]
+    dt = getattr(torch, dtype)
+    pat = torch.arange(65536, dtype=torch.int32)
+    bias = torch.where(pat >= 32768, pat - 65536, pat).to(torch.int16).view(dt).cuda()
+    x = torch.ones((1, 1, 65536), dtype=dt, device="cuda")
+    lens = torch.ones(1, dtype=torch.int32, device="cuda")
+
+    def run(taps):
+        w = torch.zeros((taps, 65536), dtype=dt, device="cuda")
+        out = torch.empty_like(x)
+        op(x, lens, w, bias, out=out)
+        torch.cuda.synchronize()
+        return out.view(torch.int16).cpu().numpy().ravel(), out.float().cpu().numpy().ravel()
+
+    direct_bits, direct = run(3)
+    assert _lib.last_kernel_variant() == "conv-any"
+    for _ in range(2):
+        for taps in (9, 15, 31):
+            bits, vals = run(taps)
+            assert _lib.last_kernel_variant() == f"conv-k{taps}"
+            nan = np.isnan(direct)
+            assert np.array_equal(np.isnan(vals), nan)
+            assert np.array_equal(bits[~nan], direct_bits[~nan]), taps
+
+
 # (channels, taps): vector-width boundaries, the pair path (C % 8 != 0) and K = 15.
 LAYOUTS = ((4, 1, "float32"), (2, 1, "float16"), (2, 1, "bfloat16"), (6, 15, "float16"),
            (6, 15, "bfloat16"), (8, 15, "float16"), (8, 15, "bfloat16"), (12, 9, "float32"),
