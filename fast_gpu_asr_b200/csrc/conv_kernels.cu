@@ -95,8 +95,9 @@ __device__ __forceinline__ typename PairOps<T>::P activate(typename PairOps<T>::
 
 // bf16 activation table. The activation's input is the sum rounded to bf16 and its output
 // is rounded to bf16, so for bf16 it is a function of 16 bits. The table holds it for
-// every bf16 of magnitude in [2^-12, 2^8) (20 binades x 128 significands, both signs):
-// 5120 entries, 10 KB of shared memory per block, computed by the same `silu` / `swoosh_r`
+// every bf16 of magnitude in [2^-12, 2^8) (20 binades x 128 significands): one 32-bit entry
+// per magnitude with act(+v) in its low half and act(-v) in its high half, 2560 entries,
+// 10 KB of shared memory per block. Entries are computed by the same `silu` / `swoosh_r`
 // code the direct path runs, so a looked-up value equals the computed one bit for bit.
 // Inputs outside the range (zeros, tiny and large magnitudes, inf, NaN) are computed.
 //
@@ -108,30 +109,33 @@ __device__ __forceinline__ typename PairOps<T>::P activate(typename PairOps<T>::
 constexpr uint32_t kLutExpLo = 115;                   // biased exponent of 2^-12
 constexpr uint32_t kLutExps = 20;                     // through 2^7 (|v| < 2^8)
 constexpr uint32_t kLutBase = kLutExpLo << 7;         // first magnitude pattern
-constexpr uint32_t kLutSpan = kLutExps << 7;          // magnitudes per sign
-constexpr int kLutEntries = 2 * static_cast<int>(kLutSpan);
-constexpr int kLutBytes = kLutEntries * 2;
+constexpr uint32_t kLutSpan = kLutExps << 7;          // magnitudes (entries)
+constexpr int kLutEntries = static_cast<int>(kLutSpan);
+constexpr int kLutBytes = kLutEntries * 4;
 
-__device__ __align__(16) uint16_t g_bf16_act_lut[2][kLutEntries];
+__device__ __align__(16) uint32_t g_bf16_act_lut[2][kLutEntries];
 __device__ unsigned int g_bf16_act_lut_ready[2];
 
-template <int kAct> __device__ __forceinline__ uint16_t lut_entry(int i) {
-    const uint32_t sign = static_cast<uint32_t>(i) >= kLutSpan ? 0x8000u : 0u;
-    const uint32_t bits = sign | (kLutBase + static_cast<uint32_t>(i) % kLutSpan);
-    const float v = __uint_as_float(bits << 16);
-    const float a = kAct == kSilu ? silu(v) : swoosh_r(v);
-    return __bfloat16_as_ushort(__float2bfloat16_rn(a));
+template <int kAct> __device__ __forceinline__ uint32_t lut_entry(int i) {
+    const float v = __uint_as_float((kLutBase + static_cast<uint32_t>(i)) << 16);
+    const float pos = kAct == kSilu ? silu(v) : swoosh_r(v);
+    const float neg = kAct == kSilu ? silu(-v) : swoosh_r(-v);
+    return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(pos))) |
+           (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(neg))) << 16);
 }
 
 template <int kAct>
-__device__ __forceinline__ __nv_bfloat162 activate_lut(__nv_bfloat162 v, const uint16_t* lut) {
+__device__ __forceinline__ __nv_bfloat162 activate_lut(__nv_bfloat162 v, const uint32_t* lut) {
     const uint32_t w = *reinterpret_cast<const uint32_t*>(&v);
-    const uint32_t o0 = (w & 0x7FFFu) - kLutBase;  // wraps above the span below the range
-    const uint32_t o1 = ((w >> 16) & 0x7FFFu) - kLutBase;
+    // Both magnitudes less the table base at once: a borrow out of the low half happens only
+    // when the low magnitude is below the base, and then the low offset is out of range.
+    const uint32_t off = (w & 0x7FFF7FFFu) - kLutBase * 0x10001u;
+    const uint32_t o0 = off & 0xFFFFu, o1 = off >> 16;
     if (o0 < kLutSpan && o1 < kLutSpan) {
-        const uint32_t lo = lut[o0 + ((w >> 15) & 1u) * kLutSpan];
-        const uint32_t hi = lut[o1 + (w >> 31) * kLutSpan];
-        const uint32_t r = lo | (hi << 16);
+        // Result bytes 0-1: the half of lut[o0] the low sign picks; bytes 2-3: the half of
+        // lut[o1] the high sign picks.
+        const uint32_t sel = 0x5410u + (((w >> 14) & 2u) | ((w >> 22) & 0x200u)) * 0x11u;
+        const uint32_t r = __byte_perm(lut[o0], lut[o1], sel);
         return *reinterpret_cast<const __nv_bfloat162*>(&r);
     }
     return activate<__nv_bfloat16, kAct>(v);
@@ -251,7 +255,7 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
     int cur_slab = -1;
     Tile cur = t_begin < t_end ? decode(t_begin) : Tile{0, 0, 0};
     if (kStages == 2 && t_begin < t_end) stage(cur, 0);
-    uint16_t* const lut = reinterpret_cast<uint16_t*>(s_dyn);
+    uint32_t* const lut = reinterpret_cast<uint32_t*>(s_dyn);
     if constexpr (kLut) {
         // Fill the activation table (under the first tile's copies).
         __shared__ unsigned int s_lut_ready;
@@ -264,7 +268,7 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
                 reinterpret_cast<uint4*>(lut)[i] = __ldcg(src + i);
         } else {
             for (int i = tid; i < kLutEntries; i += kConvThreads) {
-                const uint16_t e = lut_entry<kAct>(i);
+                const uint32_t e = lut_entry<kAct>(i);
                 lut[i] = e;
                 g_bf16_act_lut[kAct][i] = e;
             }
