@@ -21,11 +21,11 @@
 //
 // Launch shape: a warp computes kFrames consecutive output frames x 64 channels of one
 // utterance; lane l holds channel pair l of the slab, so each frame is read and written as
-// one coalesced 128-byte row (16-bit types). Each input frame is loaded once per tile and
-// applied to every output frame of the tile it reaches. Warps take equal contiguous runs
-// of the tiles ordered (channel slab, utterance, frame tile): a warp reloads weights only
-// when its slab changes, and a tile's halo frames are mostly the previous tile's, still in
-// L1.
+// one coalesced 128-byte row (16-bit types). Groups of 8 warps stage a tile's input frames
+// in shared memory once and apply each to every output frame of the tile it reaches; a
+// block holds several groups and the activation table they share. Groups take equal
+// contiguous runs of the tiles ordered (channel slab, utterance, frame tile): a group
+// reloads weights only when its slab changes.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -93,52 +93,87 @@ __device__ __forceinline__ typename PairOps<T>::P activate(typename PairOps<T>::
     else return PairOps<T>::from_float2(swoosh_r(f.x), swoosh_r(f.y));
 }
 
-// bf16 activation table. The activation's input is the sum rounded to bf16 and its output
-// is rounded to bf16, so for bf16 it is a function of 16 bits. The table holds it for
-// every bf16 of magnitude in [2^-12, 2^8) (20 binades x 128 significands): one 32-bit entry
-// per magnitude with act(+v) in its low half and act(-v) in its high half, 2560 entries,
-// 10 KB of shared memory per block. Entries are computed by the same `silu` / `swoosh_r`
-// code the direct path runs, so a looked-up value equals the computed one bit for bit.
-// Inputs outside the range (zeros, tiny and large magnitudes, inf, NaN) are computed.
+// Activation tables for the 16-bit types. The activation's input is the sum rounded to
+// the storage type and its output is rounded to it, so it is a function of 16 bits. A table
+// holds it for every magnitude in [2^e_lo, 2^e_hi) of the type: one 32-bit entry per
+// magnitude with act(+v) in its low half and act(-v) in its high half.
+//   bf16: [2^-12, 2^8), 20 binades x 128 significands  =  2560 entries, 10 KB;
+//   f16:  [2^-10, 2^4), 14 binades x 1024 significands = 14336 entries, 56 KB.
+// Entries are computed by the same `silu` / `swoosh_r` code the direct path runs, so a
+// looked-up value equals the computed one bit for bit. Inputs outside the range (zeros,
+// tiny and large magnitudes, inf, NaN) are computed. A block keeps the table in shared
+// memory for all of its warps.
 //
-// Each device holds one copy per activation in global memory, built by the first launch
-// that finds its ready flag clear: every block of that launch computes the table itself,
-// writes it to shared memory and to the global copy, and publishes the flag with a release
-// store after a fence. Later blocks that read the flag set (acquire) copy the 10 KB from
-// L2 instead. Concurrent builders write identical values.
-constexpr uint32_t kLutExpLo = 115;                   // biased exponent of 2^-12
-constexpr uint32_t kLutExps = 20;                     // through 2^7 (|v| < 2^8)
-constexpr uint32_t kLutBase = kLutExpLo << 7;         // first magnitude pattern
-constexpr uint32_t kLutSpan = kLutExps << 7;          // magnitudes (entries)
-constexpr int kLutEntries = static_cast<int>(kLutSpan);
-constexpr int kLutBytes = kLutEntries * 4;
-
-__device__ __align__(16) uint32_t g_bf16_act_lut[2][kLutEntries];
-__device__ unsigned int g_bf16_act_lut_ready[2];
-
-template <int kAct> __device__ __forceinline__ uint32_t lut_entry(int i) {
-    const float v = __uint_as_float((kLutBase + static_cast<uint32_t>(i)) << 16);
-    const float pos = kAct == kSilu ? silu(v) : swoosh_r(v);
-    const float neg = kAct == kSilu ? silu(-v) : swoosh_r(-v);
-    return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(pos))) |
-           (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(neg))) << 16);
+// Each device holds one copy per (type, activation) in global memory, built by the first
+// launch that finds its ready flag clear: every block of that launch computes the table
+// itself, writes it to shared memory and to the global copy, and publishes the flag with a
+// release store after a fence. Later blocks that read the flag set (acquire) copy the table
+// from L2 instead. Concurrent builders write identical values.
+template <typename T> struct LutSpec;
+template <> struct LutSpec<__nv_bfloat16> {
+    static constexpr uint32_t kMant = 7, kExpLo = 115, kExps = 20;  // 115: biased 2^-12
+    static __device__ __forceinline__ float to_float(uint32_t bits) {
+        return __uint_as_float(bits << 16);
+    }
+    static __device__ __forceinline__ uint32_t round(float a) {
+        return __bfloat16_as_ushort(__float2bfloat16_rn(a));
+    }
+};
+template <> struct LutSpec<__half> {
+    static constexpr uint32_t kMant = 10, kExpLo = 5, kExps = 14;  // 5: biased 2^-10
+    static __device__ __forceinline__ float to_float(uint32_t bits) {
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+    }
+    static __device__ __forceinline__ uint32_t round(float a) {
+        return __half_as_ushort(__float2half_rn(a));
+    }
+};
+template <typename T> struct Lut {
+    static constexpr uint32_t kBase = LutSpec<T>::kExpLo << LutSpec<T>::kMant;  // first magnitude
+    static constexpr uint32_t kSpan = LutSpec<T>::kExps << LutSpec<T>::kMant;   // entries
+    static constexpr int kBytes = static_cast<int>(kSpan) * 4;
+};
+template <typename T> constexpr int lut_bytes() {
+    if constexpr (sizeof(T) == 2) return Lut<T>::kBytes;
+    else return 0;
 }
 
-template <int kAct>
-__device__ __forceinline__ __nv_bfloat162 activate_lut(__nv_bfloat162 v, const uint32_t* lut) {
+__device__ __align__(16) uint32_t g_bf16_act_lut[2][Lut<__nv_bfloat16>::kSpan];
+__device__ __align__(16) uint32_t g_f16_act_lut[2][Lut<__half>::kSpan];
+__device__ unsigned int g_act_lut_ready[2][2];  // [bf16, f16][activation]
+
+template <typename T> __device__ __forceinline__ uint32_t* global_lut(int act) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) return g_bf16_act_lut[act];
+    else return g_f16_act_lut[act];
+}
+template <typename T> __device__ __forceinline__ unsigned int* lut_ready(int act) {
+    return &g_act_lut_ready[std::is_same<T, __nv_bfloat16>::value ? 0 : 1][act];
+}
+
+template <typename T, int kAct> __device__ __forceinline__ uint32_t lut_entry(int i) {
+    const float v = LutSpec<T>::to_float(Lut<T>::kBase + static_cast<uint32_t>(i));
+    const float pos = kAct == kSilu ? silu(v) : swoosh_r(v);
+    const float neg = kAct == kSilu ? silu(-v) : swoosh_r(-v);
+    return LutSpec<T>::round(pos) | (LutSpec<T>::round(neg) << 16);
+}
+
+template <typename T, int kAct>
+__device__ __forceinline__ typename PairOps<T>::P activate_lut(typename PairOps<T>::P v,
+                                                              const uint32_t* lut) {
+    constexpr uint32_t kBase = Lut<T>::kBase, kSpan = Lut<T>::kSpan;
     const uint32_t w = *reinterpret_cast<const uint32_t*>(&v);
     // Both magnitudes less the table base at once: a borrow out of the low half happens only
     // when the low magnitude is below the base, and then the low offset is out of range.
-    const uint32_t off = (w & 0x7FFF7FFFu) - kLutBase * 0x10001u;
+    const uint32_t off = (w & 0x7FFF7FFFu) - kBase * 0x10001u;
     const uint32_t o0 = off & 0xFFFFu, o1 = off >> 16;
-    if (o0 < kLutSpan && o1 < kLutSpan) {
+    if (o0 < kSpan && o1 < kSpan) {
         // Result bytes 0-1: the half of lut[o0] the low sign picks; bytes 2-3: the half of
         // lut[o1] the high sign picks.
         const uint32_t sel = 0x5410u + (((w >> 14) & 2u) | ((w >> 22) & 0x200u)) * 0x11u;
         const uint32_t r = __byte_perm(lut[o0], lut[o1], sel);
-        return *reinterpret_cast<const __nv_bfloat162*>(&r);
+        return *reinterpret_cast<const typename PairOps<T>::P*>(&r);
     }
-    return activate<__nv_bfloat16, kAct>(v);
+    return activate<T, kAct>(v);
 }
 
 template <typename T> __device__ __forceinline__ typename PairOps<T>::P load_pair(const T* p) {
@@ -149,54 +184,81 @@ template <typename T> __device__ __forceinline__ typename PairOps<T>::P load_pai
 // per pair).
 template <typename T> __host__ __device__ constexpr int frames_per_tile() { return sizeof(T) == 4 ? 8 : 16; }
 
+// Shape of the fixed-K kernel for storage type T and kK taps. A group is 8 warps (256
+// threads) computing a tile of 64 channels x kTileFrames output frames of one utterance; a
+// block holds kGroups groups (four, or three where four would not fit shared memory) and
+// the activation table they share. All shared memory is dynamic:
+//   [table (16-bit types)] [group 0: kStages input tiles, weights] [group 1 ...] ...
+template <typename T, int kK> struct ConvShape {
+    using P = typename PairOps<T>::P;
+    static constexpr int kFrames = frames_per_tile<T>();       // output frames per warp
+    static constexpr int kTileFrames = 8 * kFrames;
+    static constexpr int kRows = kTileFrames + kK - 1;           // staged input rows
+    static constexpr int kRowBytes = kSlabPairs * static_cast<int>(sizeof(P));
+    // 16-bit types stage the next tile while the current one is computed (two buffers);
+    // fp32 tiles are twice as large and use one.
+    static constexpr int kStages = sizeof(T) == 2 ? 2 : 1;
+    static constexpr int kStageBytes = kRows * kRowBytes;
+    static constexpr int kGroupBytes = kStages * kStageBytes + kK * kRowBytes;
+    static constexpr int kTableBytes = lut_bytes<T>();
+    static constexpr int kMaxSmem = 227 * 1024;
+    static constexpr int kGroups = kTableBytes + 4 * kGroupBytes <= kMaxSmem ? 4 : 3;
+    static constexpr int kThreads = 256 * kGroups;
+    static constexpr int kSmemBytes = kTableBytes + kGroups * kGroupBytes;
+    static_assert(kSmemBytes <= kMaxSmem, "convolution tile does not fit shared memory");
+};
+
 // Compile-time tap count kK (the kernel sizes of the encoders: 9, 15, 31).
 //
-// Block tile: 64 channels x kBlockFrames output frames of one utterance. The block stages
-// the tile's input frames (kBlockFrames + kK - 1 rows of 64 channels, zeros where a frame is
-// padded or outside [0, T)) and the slab's weights in shared memory, then warp w computes
-// kFrames of the output frames with lane l on channel pair l. Taps are the outer loop: for
-// tap k output frame j takes staged row j + k, so a warp's rows form a window of kFrames
-// that slides by one row per tap (one shared-memory load per tap) and every accumulator
-// receives its taps in tap order. Weights up to 15 taps stay in registers for the block's
-// run of tiles of one slab; longer kernels read each tap's weight from shared memory.
-// Four blocks per SM (64 registers): the kernel is issue-bound, and at three blocks the
-// kernel-15 instantiations (weights in registers) ran slower.
+// One block per SM. Each group of 8 warps runs the tile loop below on its own staging
+// buffers and weights, synchronised by its own named barrier, so the groups are as
+// independent as separate blocks; they share the activation table, filled once per block.
+// Groups take equal contiguous runs of the tiles ordered (channel slab, utterance, frame
+// tile). A group stages a tile's input frames (kTileFrames + kK - 1 rows of 64 channels,
+// zeros where a frame is padded or outside [0, T)) and the slab's weights, then warp w
+// computes kFrames of the output frames with lane l on channel pair l. Taps are the outer
+// loop: for tap k output frame j takes staged row j + k, so a warp's rows form a window of
+// kFrames that slides by one row per tap (one shared-memory load per tap) and every
+// accumulator receives its taps in tap order; each tap's weight is read from shared memory
+// (keeping them in registers spilled at the 64 registers per thread that four groups allow).
 template <typename T, int kK, int kAct, bool kSkip>
-__global__ void __launch_bounds__(kConvThreads, 4)
+__global__ void __launch_bounds__(ConvShape<T, kK>::kThreads, 1)
 depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
                       const T* __restrict__ w, const T* __restrict__ bias, T* __restrict__ y,
                       int batch, int seq, int channels, int tiles, int64_t tasks) {
+    using S = ConvShape<T, kK>;
     using Ops = PairOps<T>;
     using P = typename Ops::P;
-    constexpr int kFrames = frames_per_tile<T>();
-    constexpr int kBlockFrames = (kConvThreads / 32) * kFrames;
-    constexpr int kRows = kBlockFrames + kK - 1;
+    constexpr int kFrames = S::kFrames;
+    constexpr int kTileFrames = S::kTileFrames;
+    constexpr int kRows = S::kRows;
     constexpr int kPad = kK / 2;
-    constexpr int kRowBytes = kSlabPairs * static_cast<int>(sizeof(P));
+    constexpr int kRowBytes = S::kRowBytes;
     constexpr int kChunks = kRowBytes / 16;                      // 16-byte pieces of a row
     constexpr int kChunkElems = 16 / static_cast<int>(sizeof(T));
-    constexpr bool kWeightsInRegs = kK <= 15;
-    constexpr int kRegTaps = kWeightsInRegs ? kK : 1;
-    // 16-bit types stage the next tile while the current one is computed (two buffers);
-    // fp32 tiles are twice as large and use one.
-    constexpr int kStages = sizeof(T) == 2 ? 2 : 1;
-    // bf16 looks its activation up in a table (dynamic shared memory, kLutBytes).
-    constexpr bool kLut = std::is_same<T, __nv_bfloat16>::value;
-    __shared__ __align__(16) unsigned char s_x[kStages][kRows * kRowBytes];
-    __shared__ __align__(16) unsigned char s_w[kK * kRowBytes];
-    extern __shared__ __align__(16) unsigned char s_dyn[];
+    constexpr int kStages = S::kStages;
+    constexpr int kGroupThreads = 256;
+    constexpr bool kLut = sizeof(T) == 2;
+    extern __shared__ __align__(16) unsigned char smem[];
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int group = tid / kGroupThreads, gtid = tid % kGroupThreads, warp = gtid >> 5;
+    const uint32_t group_bar = 1 + static_cast<uint32_t>(group);  // 0 is __syncthreads
+    uint32_t* const lut = reinterpret_cast<uint32_t*>(smem);
+    unsigned char* const s_x = smem + S::kTableBytes + group * S::kGroupBytes;
+    unsigned char* const s_w = s_x + kStages * S::kStageBytes;
+
     const int npairs = channels / 2;
     const int64_t per_slab = static_cast<int64_t>(batch) * tiles;
-    const int64_t per = (tasks + gridDim.x - 1) / gridDim.x;
-    const int64_t t_begin = static_cast<int64_t>(blockIdx.x) * per;
+    const int64_t groups_total = static_cast<int64_t>(gridDim.x) * S::kGroups;
+    const int64_t per = (tasks + groups_total - 1) / groups_total;
+    const int64_t t_begin = (static_cast<int64_t>(blockIdx.x) * S::kGroups + group) * per;
     const int64_t t_end = t_begin + per < tasks ? t_begin + per : tasks;
     // 16-byte staging needs every row piece aligned: 8 (16-bit) or 4 (fp32) channels.
     const bool vec16 = (channels % kChunkElems) == 0 &&
                        (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 
-    // A task's (slab, utterance, frame tile): the block's first task is decoded once, each
+    // A task's (slab, utterance, frame tile): the group's first task is decoded once, each
     // next one is its predecessor advanced by one tile (no division per tile).
     struct Tile {
         int slab, n, f0;
@@ -206,12 +268,12 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         t.slab = static_cast<int>(task / per_slab);
         const int64_t rem = task - t.slab * per_slab;
         t.n = static_cast<int>(rem / tiles);
-        t.f0 = static_cast<int>(rem - static_cast<int64_t>(t.n) * tiles) * kBlockFrames;
+        t.f0 = static_cast<int>(rem - static_cast<int64_t>(t.n) * tiles) * kTileFrames;
         return t;
     };
     auto advance = [&](Tile t) {
-        t.f0 += kBlockFrames;
-        if (t.f0 >= tiles * kBlockFrames) {
+        t.f0 += kTileFrames;
+        if (t.f0 >= tiles * kTileFrames) {
             t.f0 = 0;
             if (++t.n == batch) {
                 t.n = 0;
@@ -227,10 +289,10 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         const int requested = __ldg(lens + t.n);
         const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
         const T* xb = x + static_cast<int64_t>(t.n) * seq * channels;
-        unsigned char* sx = s_x[buf];
+        unsigned char* sx = s_x + buf * S::kStageBytes;
         if (vec16) {
             const int c_slab = t.slab * 2 * kSlabPairs;
-            for (int i = tid; i < kRows * kChunks; i += kConvThreads) {
+            for (int i = gtid; i < kRows * kChunks; i += kGroupThreads) {
                 const int r = i / kChunks, c = c_slab + (i % kChunks) * kChunkElems;
                 const int fi = t.f0 - kPad + r;
                 const bool valid = static_cast<unsigned>(fi) < static_cast<unsigned>(vl) &&
@@ -239,7 +301,7 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
                 cp_async16_zfill(smem_u32(sx + i * 16), src, valid ? 16u : 0u);
             }
         } else {
-            for (int i = tid; i < kRows * kSlabPairs; i += kConvThreads) {
+            for (int i = gtid; i < kRows * kSlabPairs; i += kGroupThreads) {
                 const int r = i / kSlabPairs, q = t.slab * kSlabPairs + i % kSlabPairs;
                 const int fi = t.f0 - kPad + r;
                 P v = Ops::zero();
@@ -251,31 +313,32 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         cp_async_commit();
     };
 
-    P wr[kRegTaps], b0 = Ops::zero();
+    P b0 = Ops::zero();
     int cur_slab = -1;
     Tile cur = t_begin < t_end ? decode(t_begin) : Tile{0, 0, 0};
     if (kStages == 2 && t_begin < t_end) stage(cur, 0);
-    uint32_t* const lut = reinterpret_cast<uint32_t*>(s_dyn);
     if constexpr (kLut) {
-        // Fill the activation table (under the first tile's copies).
+        // Fill the activation table (under the first tiles' copies), all groups together.
+        constexpr int kEntries = static_cast<int>(Lut<T>::kSpan);
         __shared__ unsigned int s_lut_ready;
-        if (tid == 0) s_lut_ready = ld_acquire_gpu(&g_bf16_act_lut_ready[kAct]);
+        if (tid == 0) s_lut_ready = ld_acquire_gpu(lut_ready<T>(kAct));
         __syncthreads();
         const bool ready = s_lut_ready != 0u;
+        uint32_t* const glut = global_lut<T>(kAct);
         if (ready) {
-            const uint4* src = reinterpret_cast<const uint4*>(g_bf16_act_lut[kAct]);
-            for (int i = tid; i < kLutBytes / 16; i += kConvThreads)
+            const uint4* src = reinterpret_cast<const uint4*>(glut);
+            for (int i = tid; i < Lut<T>::kBytes / 16; i += S::kThreads)
                 reinterpret_cast<uint4*>(lut)[i] = __ldcg(src + i);
         } else {
-            for (int i = tid; i < kLutEntries; i += kConvThreads) {
-                const uint32_t e = lut_entry<kAct>(i);
+            for (int i = tid; i < kEntries; i += S::kThreads) {
+                const uint32_t e = lut_entry<T, kAct>(i);
                 lut[i] = e;
-                g_bf16_act_lut[kAct][i] = e;
+                glut[i] = e;
             }
             __threadfence();
         }
         __syncthreads();
-        if (!ready && tid == 0) st_release_gpu(&g_bf16_act_lut_ready[kAct], 1u);
+        if (!ready && tid == 0) st_release_gpu(lut_ready<T>(kAct), 1u);
     }
     int buf = 0;
     for (int64_t task = t_begin; task < t_end; ++task) {
@@ -285,13 +348,13 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         const int p = slab * kSlabPairs + lane;
         const bool ok = p < npairs;
         const bool new_slab = slab != cur_slab;
-        // Every warp finished reading the other buffer and the weights (end of the previous
-        // iteration), so they can be refilled.
+        // Every warp of the group finished reading the other buffer and the weights (end of
+        // the previous iteration), so they can be refilled.
         const bool prefetch = kStages == 2 && task + 1 < t_end;
         if (prefetch) stage(next, buf ^ 1);
         if (kStages == 1) stage(tile, 0);
         if (new_slab) {
-            for (int i = tid; i < kK * kSlabPairs; i += kConvThreads) {
+            for (int i = gtid; i < kK * kSlabPairs; i += kGroupThreads) {
                 const int k = i / kSlabPairs, q = slab * kSlabPairs + i % kSlabPairs;
                 *reinterpret_cast<P*>(s_w + i * sizeof(P)) =
                     q < npairs ? load_pair(w + static_cast<int64_t>(k) * channels + 2 * q)
@@ -303,16 +366,10 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         const int vl = requested < 0 ? 0 : (requested < seq ? requested : seq);
         if (prefetch) cp_async_wait<1>();  // this tile's group is complete
         else cp_async_wait<0>();
-        __syncthreads();
-        if constexpr (kWeightsInRegs) {
-            if (new_slab) {
-#pragma unroll
-                for (int k = 0; k < kK; ++k)
-                    wr[k] = *reinterpret_cast<const P*>(s_w + k * kRowBytes + lane * sizeof(P));
-            }
-        }
+        named_barrier(group_bar, kGroupThreads);
         const int fw = f0 + warp * kFrames;  // this warp's first output frame
-        const unsigned char* xs = s_x[buf] + warp * kFrames * kRowBytes + lane * sizeof(P);
+        const unsigned char* xs =
+            s_x + buf * S::kStageBytes + warp * kFrames * kRowBytes + lane * sizeof(P);
         P acc[kFrames], win[kFrames];
 #pragma unroll
         for (int j = 0; j < kFrames; ++j) {
@@ -321,9 +378,7 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         }
 #pragma unroll
         for (int k = 0; k < kK; ++k) {
-            P wk;
-            if constexpr (kWeightsInRegs) wk = wr[k < kRegTaps ? k : 0];
-            else wk = *reinterpret_cast<const P*>(s_w + k * kRowBytes + lane * sizeof(P));
+            const P wk = *reinterpret_cast<const P*>(s_w + k * kRowBytes + lane * sizeof(P));
             // win[(j + k) % kFrames] holds staged row j + k (input frame fw - kPad + j + k).
 #pragma unroll
             for (int j = 0; j < kFrames; ++j) {
@@ -341,17 +396,17 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
             for (int j = 0; j < kFrames; ++j)
                 if (fw + j < seq) {
                     P out;
-                    if constexpr (kLut) out = activate_lut<kAct>(acc[j], lut);
+                    if constexpr (kLut) out = activate_lut<T, kAct>(acc[j], lut);
                     else out = activate<T, kAct>(acc[j]);
                     *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) = out;
                 }
         }
         cur_slab = slab;
         cur = next;
-        __syncthreads();  // this tile's rows and the weights are read: both may be refilled
+        named_barrier(group_bar, kGroupThreads);  // this tile's rows and the weights are read
         buf ^= kStages - 1;
     }
-    cp_async_wait<0>();  // nothing left in flight (a block with no tile committed none)
+    cp_async_wait<0>();  // nothing left in flight (a group with no tile committed none)
 }
 
 // Any odd tap count: one output frame pair per thread per step, weights read per tap
@@ -387,16 +442,17 @@ depthwise_conv_any_kernel(const T* __restrict__ x, const int32_t* __restrict__ l
     }
 }
 
-// Resident blocks per SM of a kernel with `dyn_smem` bytes of dynamic shared memory,
-// looked up once per (kernel, device).
-template <typename Kernel> int blocks_per_sm(Kernel kernel, int dyn_smem = 0) {
+// Resident blocks per SM of `kKernel` launched with `threads` threads and `dyn_smem` bytes of
+// dynamic shared memory, looked up once per (kernel, device).
+template <auto kKernel> int blocks_per_sm(int threads, int dyn_smem = 0) {
     static std::atomic<int> cache[kMaxCachedDevices];
+    const auto kernel = kKernel;
     const int dev = current_device();
     if (dev >= 0 && dev < kMaxCachedDevices) {
         if (const int v = cache[dev].load(std::memory_order_relaxed)) return v;
     }
     int v = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kConvThreads, dyn_smem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, threads, dyn_smem) !=
             cudaSuccess ||
         v < 1)
         v = 1;
@@ -406,22 +462,23 @@ template <typename Kernel> int blocks_per_sm(Kernel kernel, int dyn_smem = 0) {
 
 template <typename T, int kK, int kAct, bool kSkip>
 cudaError_t launch_fixed(const ConvolutionProblem& p, cudaStream_t stream) {
-    constexpr int kBlockFrames = (kConvThreads / 32) * frames_per_tile<T>();
-    const int tiles = (p.length + kBlockFrames - 1) / kBlockFrames;
+    using S = ConvShape<T, kK>;
+    const int tiles = (p.length + S::kTileFrames - 1) / S::kTileFrames;
     const int slabs = (p.channels / 2 + kSlabPairs - 1) / kSlabPairs;
     const int64_t tasks = static_cast<int64_t>(slabs) * p.batch * tiles;
     auto kernel = depthwise_conv_kernel<T, kK, kAct, kSkip>;
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
-    constexpr int kDyn = std::is_same<T, __nv_bfloat16>::value ? kLutBytes : 0;
-    if constexpr (kDyn > 0) {
-        static SmemAttr attr;
-        const cudaError_t e = attr.ensure(reinterpret_cast<const void*>(kernel), kDyn);
-        if (e != cudaSuccess) return e;
-    }
-    int64_t grid = static_cast<int64_t>(sms) * blocks_per_sm(kernel, kDyn);
-    if (grid > tasks) grid = tasks;
-    kernel<<<static_cast<unsigned>(grid), kConvThreads, kDyn, stream>>>(
+    static SmemAttr attr;
+    const cudaError_t e = attr.ensure(reinterpret_cast<const void*>(kernel), S::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    // Enough blocks for every group to have a tile, at most the resident ones.
+    int64_t grid = static_cast<int64_t>(sms) *
+                   blocks_per_sm<depthwise_conv_kernel<T, kK, kAct, kSkip>>(S::kThreads,
+                                                                            S::kSmemBytes);
+    const int64_t needed = (tasks + S::kGroups - 1) / S::kGroups;
+    if (grid > needed) grid = needed;
+    kernel<<<static_cast<unsigned>(grid), S::kThreads, S::kSmemBytes, stream>>>(
         static_cast<const T*>(p.x), p.valid_lengths, static_cast<const T*>(p.weight),
         static_cast<const T*>(p.bias), static_cast<T*>(p.output), p.batch, p.length, p.channels,
         tiles, tasks);
@@ -434,7 +491,8 @@ cudaError_t launch_any(const ConvolutionProblem& p, cudaStream_t stream) {
     const int sms = sm_count();
     if (sms <= 0) return cudaErrorNotSupported;
     auto kernel = depthwise_conv_any_kernel<T, kAct, kSkip>;
-    int64_t grid = static_cast<int64_t>(sms) * blocks_per_sm(kernel);
+    int64_t grid =
+        static_cast<int64_t>(sms) * blocks_per_sm<depthwise_conv_any_kernel<T, kAct, kSkip>>(kConvThreads);
     const int64_t needed = (total + kConvThreads - 1) / kConvThreads;
     if (grid > needed) grid = needed;
     kernel<<<static_cast<unsigned>(grid), kConvThreads, 0, stream>>>(
