@@ -95,10 +95,13 @@ __device__ __forceinline__ typename PairOps<T>::P activate(typename PairOps<T>::
 
 // Activation tables for the 16-bit types. The activation's input is the sum rounded to
 // the storage type and its output is rounded to it, so it is a function of 16 bits. A table
-// holds it for every magnitude in [2^e_lo, 2^e_hi) of the type: one 32-bit entry per
-// magnitude with act(+v) in its low half and act(-v) in its high half.
-//   bf16: [2^-12, 2^8), 20 binades x 128 significands  =  2560 entries, 10 KB;
-//   f16:  [2^-10, 2^4), 14 binades x 1024 significands = 14336 entries, 56 KB.
+// holds it for every magnitude below 2^e_hi (bf16: from 2^-20) of the type: one 32-bit
+// entry per magnitude with act(+v) in its low half and act(-v) in its high half.
+//   bf16: [2^-20, 2^8), 28 binades x 128 significands =  3584 entries, 14 KB;
+//   f16:  [0, 2^4), zero, subnormals and 18 binades    = 19456 entries, 76 KB.
+// The ranges reach down far enough that the sums of padded frames (the bias alone) of
+// almost every channel are in them: a warp with one lane outside the range evaluates the
+// activation for that lane.
 // Entries are computed by the same `silu` / `swoosh_r` code the direct path runs, so a
 // looked-up value equals the computed one bit for bit. Inputs outside the range (zeros,
 // tiny and large magnitudes, inf, NaN) are computed. A block keeps the table in shared
@@ -111,7 +114,7 @@ __device__ __forceinline__ typename PairOps<T>::P activate(typename PairOps<T>::
 // from L2 instead. Concurrent builders write identical values.
 template <typename T> struct LutSpec;
 template <> struct LutSpec<__nv_bfloat16> {
-    static constexpr uint32_t kMant = 7, kExpLo = 115, kExps = 20;  // 115: biased 2^-12
+    static constexpr uint32_t kMant = 7, kExpLo = 107, kExps = 28;  // 107: biased 2^-20
     static __device__ __forceinline__ float to_float(uint32_t bits) {
         return __uint_as_float(bits << 16);
     }
@@ -120,7 +123,7 @@ template <> struct LutSpec<__nv_bfloat16> {
     }
 };
 template <> struct LutSpec<__half> {
-    static constexpr uint32_t kMant = 10, kExpLo = 5, kExps = 14;  // 5: biased 2^-10
+    static constexpr uint32_t kMant = 10, kExpLo = 0, kExps = 19;  // 0: zero and subnormals
     static __device__ __forceinline__ float to_float(uint32_t bits) {
         return __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
     }
