@@ -395,14 +395,26 @@ depthwise_conv_kernel(const T* __restrict__ x, const int32_t* __restrict__ lens,
         }
         if (ok) {
             T* yp = y + (static_cast<int64_t>(n) * seq + fw) * channels + 2 * p;
+            // The frame check is hoisted out of the common case (the warp's frames all
+            // below T), which leaves the loop with no per-frame range test.
+            if (fw + kFrames <= seq) {
 #pragma unroll
-            for (int j = 0; j < kFrames; ++j)
-                if (fw + j < seq) {
+                for (int j = 0; j < kFrames; ++j) {
                     P out;
                     if constexpr (kLut) out = activate_lut<T, kAct>(acc[j], lut);
                     else out = activate<T, kAct>(acc[j]);
                     *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) = out;
                 }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kFrames; ++j)
+                    if (fw + j < seq) {
+                        P out;
+                        if constexpr (kLut) out = activate_lut<T, kAct>(acc[j], lut);
+                        else out = activate<T, kAct>(acc[j]);
+                        *reinterpret_cast<P*>(yp + static_cast<int64_t>(j) * channels) = out;
+                    }
+            }
         }
         cur_slab = slab;
         cur = next;

@@ -157,6 +157,62 @@ def test_activation_table_equals_direct_evaluation(kind, dtype):
             assert np.array_equal(bits[~nan], direct_bits[~nan]), taps
 
 
+_FIRST_USE_SCRIPT = r"""
+import sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+from fast_gpu_asr_b200.convolution import parakeet_conformer_convolution, zipformer_convolution
+
+pat = torch.arange(65536, dtype=torch.int32)
+cases = []
+for op, dt in ((zipformer_convolution, torch.bfloat16), (parakeet_conformer_convolution, torch.float16)):
+    bias = torch.where(pat >= 32768, pat - 65536, pat).to(torch.int16).view(dt).cuda()
+    x = torch.ones((1, 1, 65536), dtype=dt, device="cuda")
+    lens = torch.ones(1, dtype=torch.int32, device="cuda")
+    cases.append((op, dt, bias, x, lens))
+torch.cuda.synchronize()
+streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+outs = []
+# The process's first table-driven calls, on two streams at once: both may build a table.
+for op, dt, bias, x, lens in cases:
+    for s in streams:
+        w = torch.zeros((31, 65536), dtype=dt, device="cuda")
+        o = torch.empty_like(x)
+        op(x, lens, w, bias, out=o, stream=s)
+        outs.append(o)
+torch.cuda.synchronize()
+k = 0
+for op, dt, bias, x, lens in cases:
+    ref = torch.empty_like(x)
+    op(x, lens, torch.zeros((3, 65536), dtype=dt, device="cuda"), bias, out=ref)
+    torch.cuda.synchronize()
+    rb = ref.view(torch.int16).cpu().numpy().ravel()
+    nan = np.isnan(ref.float().cpu().numpy().ravel())
+    for _ in streams:
+        got = outs[k]
+        k += 1
+        gb = got.view(torch.int16).cpu().numpy().ravel()
+        assert np.array_equal(np.isnan(got.float().cpu().numpy().ravel()), nan)
+        assert np.array_equal(gb[~nan], rb[~nan])
+print("ok")
+"""
+
+
+def test_activation_tables_built_by_concurrent_first_calls():
+    """A fresh process makes its first table-driven calls on two streams at once, so two
+    launches may build the same device table concurrently; every output must still equal
+    the direct evaluation (all 65536 inputs, bf16 Swoosh-R and f16 SiLU)."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = str(Path(__file__).resolve().parents[1])
+    r = subprocess.run([sys.executable, "-c", _FIRST_USE_SCRIPT, repo], capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
 # (channels, taps): vector-width boundaries, the pair path (C % 8 != 0) and K = 15.
 LAYOUTS = ((4, 1, "float32"), (2, 1, "float16"), (2, 1, "bfloat16"), (6, 15, "float16"),
            (6, 15, "bfloat16"), (8, 15, "float16"), (8, 15, "bfloat16"), (12, 9, "float32"),
